@@ -1,0 +1,220 @@
+"""Generate the golden vectors that pin the CPU oracle to the reference.
+
+Run once, from the repository root, with a checkout of the reference
+(Yxmura/latent) available:
+
+    python tests/golden/make_golden.py --reference <path-to-latent-checkout>
+
+The script imports the reference's own ``loader/latent_loader.py`` and
+``loader/latent_runtime.py``, feeds them seeded inputs and records inputs and
+outputs as small ``.npz`` fixtures next to this file.  The fixtures are
+committed; nothing at test or bench time needs the reference checkout.
+
+Fixtures:
+  nf4.npz      quantize_nf4 / dequantize_nf4 cases (odd counts, zero groups, g16/g32)
+  int8.npz     quantize_int8 / dequantize_int8 cases (g64 and g32)
+  mixed.npz    per-group NF4 -> INT8 fallback built from the reference's
+               encoders and SNR applied group by group
+  runtime.npz  compress_matrix artifacts (reference NPZ keys) + swiglu_expert
+               outputs, NF4 and whole-pair INT8, with/without weight_before_down
+  moe.npz      a small routed MoE layer: per-expert artifacts, x, ids (with -1
+               slots), weights, per-slot outputs of the reference swiglu_expert
+               and the fp64 top-k combine
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+
+def _ref_modules(ref_root: Path):
+    sys.path.insert(0, str(ref_root))
+    from loader import latent_loader as ll  # noqa: E402
+    from loader import latent_runtime as lr  # noqa: E402
+    return ll, lr
+
+
+def _compress(ll, name, matrix, rank, seed, force_int8=False):
+    arrays, report = ll.compress_matrix(
+        name=name, matrix=matrix, energy=0.999999, min_rank=rank, max_rank=rank,
+        group_size=32, int8_group_size=64, error_threshold=10.0,
+        snr_threshold=1e9 if force_int8 else 0.0,
+        low_snr_fraction_threshold=0.0 if force_int8 else 1.0, seed=seed)
+    assert not report.fallback
+    return arrays, report
+
+
+def _spectral(rng, m, n, r):
+    """W = U diag(s) V^T (+1e-4 noise) with Haar U, V and s_i = 0.5 i^-0.8."""
+    k = min(m, n)
+    qu, ru = np.linalg.qr(rng.standard_normal((m, k)))
+    qv, rv = np.linalg.qr(rng.standard_normal((n, k)))
+    qu *= np.sign(np.diag(ru))
+    qv *= np.sign(np.diag(rv))
+    s = 0.5 * np.arange(1, k + 1, dtype=np.float64) ** -0.8
+    w = (qu * s) @ qv.T + 1e-4 * rng.standard_normal((m, n))
+    return w.astype(np.float32)
+
+
+def make_nf4(ll):
+    rng = np.random.default_rng(11)
+    cases = [
+        (np.linspace(-2.0, 2.0, 133, dtype=np.float32).reshape(7, 19), 16),
+        (rng.standard_normal((64, 96)).astype(np.float32), 32),
+        (rng.standard_normal(33).astype(np.float32), 32),
+        (np.concatenate([np.zeros(32, np.float32), rng.standard_normal(32).astype(np.float32) * 1e-3]), 32),
+        ((rng.standard_normal((5, 64)) * np.logspace(-4, 3, 64)).astype(np.float32), 32),
+        # exact midpoints between levels exercise the argmin tie rule
+        (np.concatenate([[1.0], (ll.NF4_CODEBOOK[:-1] + ll.NF4_CODEBOOK[1:]) / 2,
+                         np.zeros(16)]).astype(np.float32), 32),
+    ]
+    out = {}
+    for i, (v, g) in enumerate(cases):
+        packed, scales, shape = ll.quantize_nf4(v, group_size=g)
+        out[f"c{i}.values"] = v
+        out[f"c{i}.group"] = np.int32(g)
+        out[f"c{i}.packed"] = packed
+        out[f"c{i}.scales"] = scales
+        out[f"c{i}.shape"] = np.array(shape, np.int64)
+        out[f"c{i}.decoded"] = ll.dequantize_nf4(packed, scales, shape, group_size=g)
+    out["n_cases"] = np.int32(len(cases))
+    np.savez_compressed(HERE / "nf4.npz", **out)
+
+
+def make_int8(ll):
+    rng = np.random.default_rng(12)
+    cases = [
+        (rng.standard_normal((64, 96)).astype(np.float32), 64),
+        (rng.standard_normal(33).astype(np.float32), 64),
+        (rng.standard_normal((16, 32)).astype(np.float32) * 50, 32),
+        (np.concatenate([np.zeros(64, np.float32), np.full(64, 0.5, np.float32)]), 64),
+    ]
+    out = {}
+    for i, (v, g) in enumerate(cases):
+        q, scales, shape = ll.quantize_int8(v, group_size=g)
+        out[f"c{i}.values"] = v
+        out[f"c{i}.group"] = np.int32(g)
+        out[f"c{i}.q"] = q
+        out[f"c{i}.scales"] = scales
+        out[f"c{i}.shape"] = np.array(shape, np.int64)
+        out[f"c{i}.decoded"] = ll.dequantize_int8(q, scales, shape, group_size=g)
+    out["n_cases"] = np.int32(len(cases))
+    np.savez_compressed(HERE / "int8.npz", **out)
+
+
+def make_mixed(ll):
+    rng = np.random.default_rng(13)
+    v = rng.standard_normal((16, 64)).astype(np.float32)
+    v[:, 5] *= 40.0   # outlier column: its groups lose SNR under NF4
+    v[3, :] *= 1e-3
+    g = 32
+    flat = v.reshape(-1, g)
+    nf4_packed, scales, is_i8, q_all, decoded = [], [], [], [], []
+    for row in flat:
+        p, s, sh = ll.quantize_nf4(row, group_size=g)
+        dq = ll.dequantize_nf4(p, s, sh, group_size=g)
+        snr = ll.quantization_snr_by_group(row, dq, g)[0]
+        nf4_packed.append(p)
+        if snr < np.float32(10.0):
+            q, s8, sh8 = ll.quantize_int8(row, group_size=g)
+            scales.append(s8[0])
+            is_i8.append(True)
+            q_all.append(q)
+            decoded.append(ll.dequantize_int8(q, s8, sh8, group_size=g))
+        else:
+            scales.append(s[0])
+            is_i8.append(False)
+            q_all.append(np.zeros(g, np.int8))
+            decoded.append(dq)
+    np.savez_compressed(
+        HERE / "mixed.npz", values=v, nf4=np.concatenate(nf4_packed),
+        scales=np.array(scales, np.float16), is_int8=np.array(is_i8),
+        int8=np.concatenate(q_all), decoded=np.concatenate(decoded).reshape(v.shape))
+
+
+def make_runtime(ll, lr):
+    rng = np.random.default_rng(14)
+    d, f, r = 64, 96, 32
+    out = {}
+    mats = {"gate": _spectral(rng, d, f, 48), "up": _spectral(rng, d, f, 48), "down": _spectral(rng, f, d, 48)}
+    for variant, force in (("nf4", False), ("int8", True)):
+        arrays = {}
+        for i, (name, m) in enumerate(mats.items()):
+            a, rep = _compress(ll, name, m, r, seed=20 + i, force_int8=force)
+            assert rep.quantization.startswith(variant), rep.quantization
+            arrays.update(a)
+        for k, val in arrays.items():
+            out[f"{variant}/{k}"] = val
+        x = rng.standard_normal((5, d)).astype(np.float32)
+        gate, up, down = (lr.load_pair(arrays, n) for n in ("gate", "up", "down"))
+        out[f"{variant}/x"] = x
+        out[f"{variant}/y"] = lr.swiglu_expert(x, gate, up, down)
+        out[f"{variant}/y_wbd"] = lr.swiglu_expert(x, gate, up, down, weight=0.3, weight_before_down=True)
+        out[f"{variant}/dense_y"] = lr.dense_swiglu_expert(x, mats["gate"], mats["up"], mats["down"])
+    for k, m in mats.items():
+        out[f"dense/{k}"] = m
+    np.savez_compressed(HERE / "runtime.npz", **out)
+
+
+def make_moe(ll, lr):
+    rng = np.random.default_rng(15)
+    E, d, f, r, T, k = 4, 64, 96, 32, 12, 2
+    out = {"E": np.int32(E), "k": np.int32(k)}
+    pairs = []
+    for e in range(E):
+        arrays = {}
+        for i, (name, (m, n)) in enumerate((("gate", (d, f)), ("up", (d, f)), ("down", (f, d)))):
+            a, _ = _compress(ll, name, _spectral(rng, m, n, 48), r, seed=100 + 3 * e + i)
+            arrays.update(a)
+        for key, val in arrays.items():
+            out[f"e{e}/{key}"] = val
+        pairs.append(tuple(lr.load_pair(arrays, n) for n in ("gate", "up", "down")))
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    logits = rng.standard_normal((T, E))
+    ids = np.argsort(-logits, axis=1)[:, :k].astype(np.int32)
+    p = np.exp(logits - logits.max(axis=1, keepdims=True))
+    w = np.take_along_axis(p, ids, axis=1)
+    w = (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
+    ids[2, 1] = -1          # skipped slots contribute nothing
+    ids[7, 0] = -1
+    per_slot = np.zeros((T, k, d), np.float32)
+    per_slot_wbd = np.zeros((T, k, d), np.float32)
+    for t in range(T):
+        for j in range(k):
+            e = ids[t, j]
+            if e < 0:
+                continue
+            g, u, dn = pairs[e]
+            per_slot[t, j] = lr.swiglu_expert(x[t:t + 1], g, u, dn)[0]
+            per_slot_wbd[t, j] = lr.swiglu_expert(x[t:t + 1], g, u, dn, weight=float(w[t, j]),
+                                                  weight_before_down=True)[0]
+    live = (ids >= 0)[:, :, None]
+    out.update(x=x, ids=ids, weights=w, per_slot=per_slot, per_slot_wbd=per_slot_wbd,
+               out=(per_slot.astype(np.float64) * w[:, :, None] * live).sum(axis=1).astype(np.float32),
+               out_wbd=(per_slot_wbd.astype(np.float64) * live).sum(axis=1).astype(np.float32))
+    np.savez_compressed(HERE / "moe.npz", **out)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, type=Path, help="checkout of Yxmura/latent")
+    args = ap.parse_args()
+    ll, lr = _ref_modules(args.reference)
+    make_nf4(ll)
+    make_int8(ll)
+    make_mixed(ll)
+    make_runtime(ll, lr)
+    make_moe(ll, lr)
+    for p in sorted(HERE.glob("*.npz")):
+        print(p.name, p.stat().st_size)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
