@@ -1,0 +1,355 @@
+#!/usr/bin/env python3
+"""Benchmark of the fused latent expert FFN (BASELINE metric: routed tokens/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+A step is one pass of the hot path -- routing, the four-phase latent SwiGLU
+chain over every routed (token, expert) pair and the top-k combine -- over
+one batch of the config's synthetic layer (``latent_b200.synth``, seeded).
+Default workload: config 1 (DeepSeek-V2-Lite-shaped decode: 64 experts,
+d=2048, f=1408, rank 256, top-6, 32 tokens, bf16 activations).
+
+``value``: routed pairs (id >= 0) of all ranks / max-over-ranks mean device
+time per step, inputs resident in HBM, L2 flushed (256 MiB write) before every
+step outside the timed events.  ``e2e``: the same metric through the public
+op with pinned host buffers: H2D of x/ids/weights and D2H of the output are
+inside the timed region.  ``roofline``: the dominant kernel's algorithmic
+bytes / its mean duration (CUDA events recorded between the library's kernel
+launches), against MEASURED_PEAKS.json.  ``cpu_baseline`` / ``--impl
+reference``: the reference CPU runtime's algorithm (the numpy oracle port)
+on the host cores.
+"""
+
+from __future__ import annotations
+
+import os
+
+_NCPU = os.cpu_count() or 1
+for _v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+    os.environ.setdefault(_v, str(_NCPU))
+
+import argparse
+import datetime
+import json
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "latent MoE-FFN routed tokens/s/GPU, decode & prefill; % HBM/tensor roofline"
+UNIT = "routed tokens/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bound on the CPU baseline's timed work")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.25)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def allreduce_max(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def allreduce_sum(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+PHASES = ["route", "phase1 x.[A_g|A_u]", "phase2 silu(t_g.B_g)*(t_u.B_u)", "phase3 h.A_d", "phase4 s.B_d",
+          "combine"]
+PHASE_KINDS = {1: ("gate_a", "up_a"), 2: ("gate_b", "up_b"), 3: ("down_a",), 4: ("down_b",)}
+
+
+def workload(cfg_id: int, device, rank: int = 0):
+    from latent_b200 import synth
+    cfg = synth.CONFIGS[cfg_id]
+    t0 = time.perf_counter()
+    es = synth.make_expert_set(cfg, device=device)
+    x, ids, w = synth.make_batch(cfg, device, seed_offset=rank)
+    torch.cuda.synchronize()
+    return cfg, es, x, ids, w, time.perf_counter() - t0
+
+
+def kind_bytes(es, kinds, experts):
+    return sum(es[k].nbytes(experts) + es[k].int8_bytes(experts) for k in kinds)
+
+
+def config_json(cfg, ids, world, parallel):
+    routed = int((ids >= 0).sum())
+    return {"workload": cfg.name, "n_expert": cfg.n_expert, "n_embd": cfg.n_embd, "n_ff": cfg.n_ff,
+            "rank": cfg.rank, "top_k": cfg.top_k, "tokens_per_gpu": int(ids.shape[0]),
+            "routed_per_gpu": routed, "x_dtype": str(cfg.x_dtype).replace("torch.", ""),
+            "quant": "NF4 g32 + per-group INT8 below 20 dB", "l2": "flushed (256 MiB write) before every step",
+            "parallelism": parallel, "seed": cfg.seed}
+
+
+def cpu_leg(cfg, es, x, ids, w, seconds: float, min_steps: int = 3):
+    """The reference runtime's algorithm (oracle port, numpy) on the host cores: steady-state forward
+    over the batch with factors pre-dequantized (the dequant time is reported separately)."""
+    import oracle as O
+    touched = sorted(set(ids[ids >= 0].cpu().tolist()))
+    t0 = time.perf_counter()
+    table = [None] * cfg.n_expert
+    for e in touched:
+        pairs = []
+        for n in ("gate", "up", "down"):
+            fa, fb = es[f"{n}_a"].expert(e), es[f"{n}_b"].expert(e)
+            pairs.append(tuple(O.decode_grouped(f.lo.numpy(), f.hi.numpy(), f.scales.numpy().view(np.uint16),
+                                                f.is_int8.numpy(), f.rows, f.cols) for f in (fa, fb)))
+        table[e] = tuple(pairs)
+    dequant_s = time.perf_counter() - t0
+    xs, ids_np, w_np = x.float().cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy()
+    O.moe_forward(xs, ids_np, w_np, table)      # warm-up
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < min_steps or (time.perf_counter() - t_start) < seconds:
+        t1 = time.perf_counter()
+        O.moe_forward(xs, ids_np, w_np, table)
+        times.append(time.perf_counter() - t1)
+        if len(times) >= 10000:
+            break
+    routed = int((ids >= 0).sum())
+    step = statistics.mean(times)
+    return {"value": routed / step, "unit": UNIT, "cores": _NCPU, "kind": "port",
+            "sample": f"{len(times)} full batches of {ids.shape[0]} tokens ({routed} routed pairs), "
+                      f"{len(touched)} experts pre-dequantized in {dequant_s:.2f} s",
+            "ms_per_step": step * 1e3, "dequant_s": dequant_s}
+
+
+def run_ours(args, world, rank, local):
+    from latent_b200 import ExpertFFN
+    dev = torch.device("cuda", local)
+    cfg, es, x, ids, w, gen_s = workload(args.config, dev, rank)
+    op = ExpertFFN(es, path="decode")
+    R = int(ids.shape[0] * ids.shape[1])
+    routed = int((ids >= 0).sum())
+    touched = sorted(set(ids[ids >= 0].cpu().tolist()))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    n_marks = len(PHASES) + 1
+    for _ in range(max(args.warmup, 3)):
+        op(x, ids, w)
+    op.check()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_marks)] for _ in range(args.steps)]
+    for row in evs:
+        for e in row:
+            e.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    for k in range(args.steps):
+        flush.zero_()
+        op.call_timed(x, ids, w, evs[k])
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    seg = np.array([[evs[k][i].elapsed_time(evs[k][i + 1]) for i in range(n_marks - 1)] for k in range(args.steps)])
+    total = seg.sum(axis=1)
+    ms = allreduce_max(float(total.mean()), world)
+    routed_all = allreduce_sum(float(routed), world)
+    phase_ms = seg.mean(axis=0)
+
+    # e2e through the op with pinned host buffers
+    hx = x.cpu().pin_memory()
+    hids = ids.cpu().pin_memory()
+    hw = w.cpu().pin_memory()
+    hout = torch.empty((x.shape[0], cfg.n_embd), dtype=torch.float32).pin_memory()
+    dx, dids, dw = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(w)
+    dout = torch.empty((x.shape[0], cfg.n_embd), dtype=torch.float32, device=dev)
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for k in range(args.warmup + args.steps):
+        flush.zero_()
+        if k >= args.warmup:
+            e2e_ev[k - args.warmup][0].record()
+        dx.copy_(hx, non_blocking=True)
+        dids.copy_(hids, non_blocking=True)
+        dw.copy_(hw, non_blocking=True)
+        op(dx, dids, dw, out=dout)
+        hout.copy_(dout, non_blocking=True)
+        if k >= args.warmup:
+            e2e_ev[k - args.warmup][1].record()
+    torch.cuda.synchronize()
+    e2e_ms = allreduce_max(statistics.mean(a.elapsed_time(b) for a, b in e2e_ev), world)
+    ref_out = op(x, ids, w)
+    torch.cuda.synchronize()
+    assert torch.equal(hout, ref_out.cpu()), "e2e output differs from the device-resident run"
+
+    pk = peaks()
+    bytes_phase = {i: kind_bytes(es, PHASE_KINDS[i], touched) for i in PHASE_KINDS}
+    x_bytes = x.numel() * x.element_size()
+    out_bytes = x.shape[0] * cfg.n_embd * 4
+    bytes_phase[1] += x_bytes
+    bytes_phase[4] += out_bytes
+    dom = max(PHASE_KINDS, key=lambda i: phase_ms[i])
+    ach = bytes_phase[dom] / (phase_ms[dom] * 1e-3) / 1e9
+    op_bytes = sum(bytes_phase.values())
+    op_ach = op_bytes / (total.mean() * 1e-3) / 1e9
+    per_route_kernels = 1 if R <= 4096 else 3
+    line = {
+        "metric": METRIC, "value": routed_all / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE recipe)",
+        "config": config_json(cfg, ids, world, "replicas" if world > 1 else "single GPU"),
+        "roofline": {"bound": "hbm", "kernel": PHASES[dom], "achieved": ach, "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "traffic": None,
+                     "algorithmic_bytes": bytes_phase[dom], "mean_ms": float(phase_ms[dom]),
+                     "peak_source": pk["source"]},
+        "roofline_op": {"achieved": op_ach, "frac": op_ach / pk["hbm_gbs"], "unit": "GB/s",
+                        "algorithmic_bytes": op_bytes, "touched_experts": len(touched)},
+        "phase_ms": {PHASES[i]: float(phase_ms[i]) for i in range(len(PHASES))},
+        "e2e": {"value": routed_all / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(hx.numel() * hx.element_size() + hids.numel() * 4 + hw.numel() * 4),
+                "d2h_bytes_per_step": int(hout.numel() * 4)},
+        "gpu_launches": args.steps * (per_route_kernels + 5),
+        "clocks": clk,
+        "gen_s": gen_s,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_leg(cfg, es, x, ids, w, args.cpu_seconds)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    return line
+
+
+def run_reference(args, world, rank, local):
+    if rank != 0:
+        return None
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    cfg, es, x, ids, w, gen_s = workload(args.config, dev, 0)
+    cb = cpu_leg(cfg, es, x, ids, w, seconds=0.0, min_steps=args.warmup + args.steps)
+    value = cb["value"]
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE recipe)",
+        "config": config_json(cfg, ids, world, "host CPU"),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cb["cores"], "kind": "port", "sample": cb["sample"]},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> int:
+    args = parse_args()
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        line = run_reference(args, world, rank, local) if args.impl == "reference" else run_ours(args, world, rank, local)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

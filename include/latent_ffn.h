@@ -1,0 +1,182 @@
+/*
+ * latent_ffn.h -- C ABI of the B200 fused latent expert FFN.
+ *
+ * Drop-in for LATENT's GGML_OP_LATENT_EXPERT_FFN device op.  The reference
+ * op is the host wrapper ggml_cuda_latent_expert_ffn (reference
+ * kernels/latent_fused_expert_ffn.cu:134-292) over the structs in
+ * kernels/latent_fused_expert_ffn.h:23-59; its CPU semantics are
+ * loader/latent_runtime.py:13-73.  Everything here is plain C: pointers,
+ * sizes, status codes.  No allocation happens inside any entry point: the
+ * caller owns every buffer, including the workspace whose size
+ * latent_expert_ffn_workspace_size() reports.  No entry point throws or
+ * aborts; all return a latent_status.
+ *
+ * Factor storage ("stacked" layout, one tensor per factor kind, all experts
+ * contiguous -- the per-expert stacking of the reference GGUF writer,
+ * loader/write_latent_gguf.py:101-123 and 230-255, with the nibble packing
+ * it actually writes):
+ *   codes   uint8  [n_expert][rows][cols/2]   two 4-bit codes per byte, the
+ *                                              even column in the low nibble
+ *                                              (loader/latent_loader.py:129)
+ *   scales  fp16   [n_expert][rows][cols/32]  one scale per 32-element group
+ *                                              along a row
+ *   NF4 group:  value = NF4_LEVEL[code] * float(scale)
+ *   INT8 group: value = float(int8(hi << 4 | lo)) * float(scale), where lo is
+ *               the 4-bit code in `codes` and hi comes from `i8_hi`.
+ *   i8_mask uint32 [n_expert][mask_words]     bit g%32 of word g/32 set when
+ *                                              expert-local group g (= row *
+ *                                              cols/32 + col/32) is INT8;
+ *                                              mask_words = ceil(rows*cols/1024)
+ *   i8_base uint32 [n_expert][mask_words]     number of INT8 groups in the
+ *                                              whole tensor before word w
+ *   i8_hi   uint8  [n_int8_groups][16]        high nibbles, same nibble order
+ * i8_mask/i8_base/i8_hi are NULL when no group is INT8.
+ * cols must be a multiple of 32 and rows*cols/2 bytes per expert; the rank
+ * dimension may be zero-padded (code 7 = 0.0, scale 1.0), which leaves every
+ * result unchanged.
+ */
+#ifndef LATENT_FFN_H
+#define LATENT_FFN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct CUstream_st; /* cudaStream_t */
+struct CUevent_st;  /* cudaEvent_t */
+
+#if defined(__GNUC__)
+#define LATENT_API __attribute__((visibility("default")))
+#else
+#define LATENT_API
+#endif
+
+#define LATENT_ABI_VERSION 1
+
+typedef enum latent_status {
+    LATENT_OK = 0,
+    LATENT_ERR_INVALID = 1,     /* NULL pointer or negative size */
+    LATENT_ERR_SHAPE = 2,       /* inconsistent or unsupported shape */
+    LATENT_ERR_DTYPE = 3,       /* unsupported x / weight / output type */
+    LATENT_ERR_ALIGN = 4,       /* buffer not aligned as required */
+    LATENT_ERR_EXPERT_ID = 5,   /* an expert id >= n_expert was routed */
+    LATENT_ERR_WORKSPACE = 6,   /* workspace missing or too small */
+    LATENT_ERR_TIMEOUT = 7,     /* a bounded device-side wait gave up */
+    LATENT_ERR_CUDA = 8,        /* a CUDA runtime call failed */
+    LATENT_ERR_UNSUPPORTED = 9  /* valid request this build does not serve */
+} latent_status;
+
+typedef enum latent_type {
+    LATENT_TYPE_F32 = 0,
+    LATENT_TYPE_F16 = 1,
+    LATENT_TYPE_BF16 = 2
+} latent_type;
+
+enum {
+    /* multiply the SwiGLU hidden by the router weight before the down
+     * projection (DeepSeek-V4; loader/latent_runtime.py:57-58) instead of in
+     * the top-k combine */
+    LATENT_FLAG_WEIGHT_BEFORE_DOWN = 1u << 0,
+    /* write per-slot rows out[T][k][d] (the ggml op's dst,
+     * kernels/latent_fused_expert_ffn.cu:259) instead of the combined
+     * out[T][d]; rows of skipped slots (id < 0) are zero */
+    LATENT_FLAG_OUT_PER_SLOT = 1u << 1
+};
+
+typedef enum latent_path {
+    LATENT_PATH_AUTO = 0,    /* pick by routed pairs per expert */
+    LATENT_PATH_DECODE = 1,  /* fp32 CUDA-core GEMV chain (rel-L2 <= 1e-5) */
+    LATENT_PATH_PREFILL = 2  /* tcgen05 f16 MMA, fp32 accumulate (rel-L2 <= 2e-3) */
+} latent_path;
+
+/* One stacked factor tensor (see the layout above).  Mirrors
+ * latent_nf4_matrix (reference kernels/latent_fused_expert_ffn.h:23-29),
+ * stacked over experts and extended with the INT8 side tables. */
+typedef struct latent_qmatrix {
+    const uint8_t *codes;
+    const uint16_t *scales;
+    const uint32_t *i8_mask;
+    const uint32_t *i8_base;
+    const uint8_t *i8_hi;
+    int64_t rows;
+    int64_t cols;
+} latent_qmatrix;
+
+/* One fused expert-FFN call.  Mirrors latent_dispatch_args
+ * (reference kernels/latent_fused_expert_ffn.h:40-50) for a whole batch of
+ * tokens, with the 15 op sources of ggml_cuda_latent_expert_ffn
+ * (kernels/latent_fused_expert_ffn.cu:135-150) as fields. */
+typedef struct latent_ffn_desc {
+    int32_t n_expert;   /* E */
+    int32_t n_embd;     /* d  (multiple of 32) */
+    int32_t n_ff;       /* f  (multiple of 32) */
+    int32_t rank;       /* r  padded rank (32, 64, 128, 256, 512 or 1024) */
+    int32_t n_tokens;   /* T  (0 allowed) */
+    int32_t top_k;      /* k */
+    int32_t x_type;     /* latent_type of x */
+    int32_t w_type;     /* latent_type of weights (F32 or F16) */
+    uint32_t flags;     /* LATENT_FLAG_* */
+    int32_t path;       /* latent_path */
+    const void *x;          /* [T][d] */
+    const int32_t *ids;     /* [T][k]; id < 0 skips the slot */
+    const void *weights;    /* [T][k] router weights */
+    float *out;             /* [T][d], or [T][k][d] with OUT_PER_SLOT */
+    latent_qmatrix gate_a;  /* rows d, cols r */
+    latent_qmatrix gate_b;  /* rows r, cols f */
+    latent_qmatrix up_a;    /* rows d, cols r */
+    latent_qmatrix up_b;    /* rows r, cols f */
+    latent_qmatrix down_a;  /* rows f, cols r */
+    latent_qmatrix down_b;  /* rows r, cols d */
+    void *workspace;        /* 256-byte aligned, latent_expert_ffn_workspace_size() bytes */
+    size_t workspace_bytes;
+} latent_ffn_desc;
+
+/* ABI version of the loaded library (LATENT_ABI_VERSION). */
+LATENT_API int latent_abi_version(void);
+
+/* Static description of a status code. */
+LATENT_API const char *latent_status_string(int status);
+
+/* Workspace bytes latent_expert_ffn_forward needs for this descriptor
+ * (pointers may be NULL here).  Replaces the per-call cudaMallocAsync of the
+ * reference wrapper (kernels/latent_fused_expert_ffn.cu:246-264). */
+LATENT_API int latent_expert_ffn_workspace_size(const latent_ffn_desc *desc, size_t *bytes);
+
+/* Routed SwiGLU expert FFN + top-k combine, stream-ordered on `stream`.
+ * Replaces ggml_cuda_latent_expert_ffn (kernels/latent_fused_expert_ffn.cu:134)
+ * and latent_fused_expert_dispatch / latent_expert_reduce (:27-132).
+ * Semantics: loader/latent_runtime.py:48-59 per routed slot, then
+ * out[t] = sum_j w[t][j] * y_j (plain sum with WEIGHT_BEFORE_DOWN).
+ * Host-side validation errors return before anything is launched.  A routed
+ * id >= n_expert is skipped and recorded in the workspace; read it with
+ * latent_expert_ffn_check(). */
+LATENT_API int latent_expert_ffn_forward(const latent_ffn_desc *desc, struct CUstream_st *stream);
+
+/* latent_expert_ffn_forward that also records the caller's events on
+ * `stream` around each kernel it launches: events[0] before routing, then one
+ * after routing and after every FFN kernel (decode: 4 phases + combine, so 7
+ * events in all).  A profiling aid with no counterpart in the reference op;
+ * results are identical to latent_expert_ffn_forward. */
+LATENT_API int latent_expert_ffn_forward_timed(const latent_ffn_desc *desc, struct CUstream_st *stream,
+                                               struct CUevent_st *const *events, int n_events);
+
+/* Synchronises `stream` and reports device-side errors recorded by the last
+ * forward that used `workspace` (LATENT_ERR_EXPERT_ID, LATENT_ERR_TIMEOUT). */
+LATENT_API int latent_expert_ffn_check(const latent_ffn_desc *desc, struct CUstream_st *stream);
+
+/* Dequantize expert `expert` of one stacked factor to fp32 out[rows][cols],
+ * bit-exact with dequantize_nf4 / dequantize_int8
+ * (reference loader/latent_loader.py:133-145, 161-170). */
+LATENT_API int latent_dequantize(const latent_qmatrix *m, int32_t expert, float *out, struct CUstream_st *stream);
+
+/* y = silu(x) elementwise in fp32 (reference loader/latent_runtime.py:39-45). */
+LATENT_API int latent_silu(const float *x, float *y, int64_t n, struct CUstream_st *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LATENT_FFN_H */

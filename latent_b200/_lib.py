@@ -1,0 +1,116 @@
+"""ctypes binding of the C ABI in ``include/latent_ffn.h``.
+
+The structs below mirror the header field for field.  The library is loaded
+from ``latent_b200/_lib/liblatent_b200.so`` (built in-tree by
+``python -m latent_b200.build``); there is no fallback -- a missing or
+unloadable library raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "liblatent_b200.so"
+
+LATENT_OK = 0
+STATUS_NAMES = {
+    0: "LATENT_OK", 1: "LATENT_ERR_INVALID", 2: "LATENT_ERR_SHAPE", 3: "LATENT_ERR_DTYPE",
+    4: "LATENT_ERR_ALIGN", 5: "LATENT_ERR_EXPERT_ID", 6: "LATENT_ERR_WORKSPACE",
+    7: "LATENT_ERR_TIMEOUT", 8: "LATENT_ERR_CUDA", 9: "LATENT_ERR_UNSUPPORTED",
+}
+
+TYPE_F32, TYPE_F16, TYPE_BF16 = 0, 1, 2
+FLAG_WEIGHT_BEFORE_DOWN = 1 << 0
+FLAG_OUT_PER_SLOT = 1 << 1
+PATH_AUTO, PATH_DECODE, PATH_PREFILL = 0, 1, 2
+
+# Every entry point the header declares, with (restype, argtypes).
+EXPORTS = {}
+
+
+class QMatrix(C.Structure):
+    _fields_ = [
+        ("codes", C.c_void_p),
+        ("scales", C.c_void_p),
+        ("i8_mask", C.c_void_p),
+        ("i8_base", C.c_void_p),
+        ("i8_hi", C.c_void_p),
+        ("rows", C.c_int64),
+        ("cols", C.c_int64),
+    ]
+
+
+class FfnDesc(C.Structure):
+    _fields_ = [
+        ("n_expert", C.c_int32),
+        ("n_embd", C.c_int32),
+        ("n_ff", C.c_int32),
+        ("rank", C.c_int32),
+        ("n_tokens", C.c_int32),
+        ("top_k", C.c_int32),
+        ("x_type", C.c_int32),
+        ("w_type", C.c_int32),
+        ("flags", C.c_uint32),
+        ("path", C.c_int32),
+        ("x", C.c_void_p),
+        ("ids", C.c_void_p),
+        ("weights", C.c_void_p),
+        ("out", C.c_void_p),
+        ("gate_a", QMatrix),
+        ("gate_b", QMatrix),
+        ("up_a", QMatrix),
+        ("up_b", QMatrix),
+        ("down_a", QMatrix),
+        ("down_b", QMatrix),
+        ("workspace", C.c_void_p),
+        ("workspace_bytes", C.c_size_t),
+    ]
+
+
+EXPORTS.update({
+    "latent_abi_version": (C.c_int, []),
+    "latent_status_string": (C.c_char_p, [C.c_int]),
+    "latent_expert_ffn_workspace_size": (C.c_int, [C.POINTER(FfnDesc), C.POINTER(C.c_size_t)]),
+    "latent_expert_ffn_forward": (C.c_int, [C.POINTER(FfnDesc), C.c_void_p]),
+    "latent_expert_ffn_check": (C.c_int, [C.POINTER(FfnDesc), C.c_void_p]),
+    "latent_expert_ffn_forward_timed": (C.c_int, [C.POINTER(FfnDesc), C.c_void_p, C.POINTER(C.c_void_p), C.c_int]),
+    "latent_dequantize": (C.c_int, [C.POINTER(QMatrix), C.c_int32, C.c_void_p, C.c_void_p]),
+    "latent_silu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
+})
+
+_lock = threading.Lock()
+_lib = None
+
+
+class LatentError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        name = STATUS_NAMES.get(status, str(status))
+        super().__init__(f"{what}: {name}" if what else name)
+
+
+def lib() -> C.CDLL:
+    """The loaded CUDA library (raises if it is missing or stale)."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `python -m latent_b200.build` "
+                    "(latent_b200 has no CPU fallback)")
+            h = C.CDLL(str(LIB_PATH))
+            for name, (res, args) in EXPORTS.items():
+                fn = getattr(h, name)
+                fn.restype = res
+                fn.argtypes = args
+            if h.latent_abi_version() != 1:
+                raise RuntimeError("liblatent_b200.so ABI version mismatch")
+            _lib = h
+    return _lib
+
+
+def check(status: int, what: str = "") -> None:
+    if status != LATENT_OK:
+        raise LatentError(status, what)

@@ -1,0 +1,267 @@
+// C-ABI entry points (include/latent_ffn.h): validation, workspace layout,
+// launch sequencing.  Nothing here allocates device memory.
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "internal.h"
+
+namespace latent {
+
+cudaError_t ensure_smem(const void *func, size_t bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    static std::mutex mu;
+    static std::map<std::pair<const void *, int>, size_t> done;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t &have = done[{func, dev}];
+    if (have >= bytes) return cudaSuccess;
+    err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (err == cudaSuccess) have = bytes;
+    return err;
+}
+
+namespace {
+
+constexpr size_t kAlign = 256;
+
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+struct Layout {
+    size_t err, counts, offsets, active, n_active, sem, order, pos, block_counts, scratch, total;
+    int n_sem;
+};
+
+bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+int check_qmatrix(const latent_qmatrix &m, int64_t rows, int64_t cols, bool need_ptrs) {
+    if (m.rows != rows || m.cols != cols) return LATENT_ERR_SHAPE;
+    if (!need_ptrs) return LATENT_OK;
+    if (!m.codes || !m.scales) return LATENT_ERR_INVALID;
+    if (!aligned(m.codes, 16) || !aligned(m.scales, 4)) return LATENT_ERR_ALIGN;
+    const bool any = m.i8_mask || m.i8_base || m.i8_hi;
+    if (any && !(m.i8_mask && m.i8_base && m.i8_hi)) return LATENT_ERR_INVALID;
+    if (m.i8_hi && !aligned(m.i8_hi, 16)) return LATENT_ERR_ALIGN;
+    return LATENT_OK;
+}
+
+bool rank_supported(int r) { return r == 32 || r == 64 || r == 128 || r == 256 || r == 512; }
+
+// Shape/type validation; `need_ptrs` also checks pointers and alignment.
+int validate(const latent_ffn_desc *d, bool need_ptrs) {
+    if (!d) return LATENT_ERR_INVALID;
+    if (d->n_expert < 1 || d->n_expert > kMaxExperts) return LATENT_ERR_SHAPE;
+    if (d->n_embd < 32 || d->n_embd % 32 || d->n_ff < 32 || d->n_ff % 32) return LATENT_ERR_SHAPE;
+    if (d->n_tokens < 0 || d->top_k < 1) return LATENT_ERR_SHAPE;
+    if ((int64_t)d->n_tokens * d->top_k > (int64_t)1 << 30) return LATENT_ERR_SHAPE;
+    if (!rank_supported(d->rank)) return LATENT_ERR_UNSUPPORTED;
+    if (d->x_type != LATENT_TYPE_F32 && d->x_type != LATENT_TYPE_F16 && d->x_type != LATENT_TYPE_BF16)
+        return LATENT_ERR_DTYPE;
+    if (d->w_type != LATENT_TYPE_F32 && d->w_type != LATENT_TYPE_F16) return LATENT_ERR_DTYPE;
+    if (d->flags & ~(uint32_t)(LATENT_FLAG_WEIGHT_BEFORE_DOWN | LATENT_FLAG_OUT_PER_SLOT)) return LATENT_ERR_INVALID;
+    if (d->path != LATENT_PATH_AUTO && d->path != LATENT_PATH_DECODE && d->path != LATENT_PATH_PREFILL)
+        return LATENT_ERR_INVALID;
+    const int64_t D = d->n_embd, F = d->n_ff, R = d->rank;
+    const bool ptrs = need_ptrs && d->n_tokens > 0;
+    int st;
+    if ((st = check_qmatrix(d->gate_a, D, R, ptrs))) return st;
+    if ((st = check_qmatrix(d->up_a, D, R, ptrs))) return st;
+    if ((st = check_qmatrix(d->gate_b, R, F, ptrs))) return st;
+    if ((st = check_qmatrix(d->up_b, R, F, ptrs))) return st;
+    if ((st = check_qmatrix(d->down_a, F, R, ptrs))) return st;
+    if ((st = check_qmatrix(d->down_b, R, D, ptrs))) return st;
+    if (ptrs) {
+        if (!d->x || !d->ids || !d->weights || !d->out) return LATENT_ERR_INVALID;
+        const size_t xs = d->x_type == LATENT_TYPE_F32 ? 4 : 2;
+        if (!aligned(d->x, xs) || !aligned(d->ids, 4) || !aligned(d->weights, d->w_type == LATENT_TYPE_F32 ? 4 : 2))
+            return LATENT_ERR_ALIGN;
+        if (!aligned(d->out, 16)) return LATENT_ERR_ALIGN;
+    }
+    return LATENT_OK;
+}
+
+int pick_path(const latent_ffn_desc *d) {
+    if (d->path != LATENT_PATH_AUTO) return d->path;
+    return LATENT_PATH_DECODE;
+}
+
+DecodeArgs decode_args(const latent_ffn_desc *d) {
+    DecodeArgs a{};
+    a.E = d->n_expert;
+    a.d = d->n_embd;
+    a.f = d->n_ff;
+    a.r = d->rank;
+    a.T = d->n_tokens;
+    a.k = d->top_k;
+    a.x_type = d->x_type;
+    a.w_type = d->w_type;
+    a.flags = d->flags;
+    a.x = d->x;
+    a.weights = d->weights;
+    a.out = d->out;
+    a.gate_a = d->gate_a;
+    a.gate_b = d->gate_b;
+    a.up_a = d->up_a;
+    a.up_b = d->up_b;
+    a.down_a = d->down_a;
+    a.down_b = d->down_b;
+    decode_plan(a);
+    return a;
+}
+
+Layout layout(const latent_ffn_desc *d, const DecodeArgs &a) {
+    Layout L{};
+    const size_t E = (size_t)d->n_expert, R = (size_t)d->n_tokens * (size_t)d->top_k;
+    size_t o = 0;
+    L.err = o;           o = align_up(o + 16);
+    L.counts = o;        o = align_up(o + E * 4);
+    L.offsets = o;       o = align_up(o + (E + 1) * 4);
+    L.active = o;        o = align_up(o + E * 4);
+    L.n_active = o;      o = align_up(o + 4);
+    L.n_sem = (int)(2 * E);
+    L.sem = o;           o = align_up(o + (size_t)L.n_sem * 4);
+    L.order = o;         o = align_up(o + R * 4);
+    L.pos = o;           o = align_up(o + R * 4);
+    L.block_counts = o;  o = align_up(o + route_block_counts_bytes((int)E, (int)R));
+    L.scratch = o;
+    o = align_up(o + decode_scratch_floats(a) * sizeof(float));
+    L.total = o;
+    return L;
+}
+
+template <class T>
+T *at(void *base, size_t off) {
+    return reinterpret_cast<T *>(static_cast<char *>(base) + off);
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? LATENT_OK : LATENT_ERR_CUDA; }
+
+}  // namespace
+
+}  // namespace latent
+
+using namespace latent;
+
+extern "C" LATENT_API int latent_abi_version(void) { return LATENT_ABI_VERSION; }
+
+extern "C" LATENT_API const char *latent_status_string(int status) {
+    switch (status) {
+        case LATENT_OK: return "ok";
+        case LATENT_ERR_INVALID: return "invalid argument (NULL pointer, bad flag or negative size)";
+        case LATENT_ERR_SHAPE: return "inconsistent or unsupported shape";
+        case LATENT_ERR_DTYPE: return "unsupported data type";
+        case LATENT_ERR_ALIGN: return "buffer not aligned as required";
+        case LATENT_ERR_EXPERT_ID: return "routed expert id >= n_expert";
+        case LATENT_ERR_WORKSPACE: return "workspace missing or too small";
+        case LATENT_ERR_TIMEOUT: return "bounded device wait timed out";
+        case LATENT_ERR_CUDA: return "CUDA runtime error";
+        case LATENT_ERR_UNSUPPORTED: return "request not supported by this build";
+        default: return "unknown status";
+    }
+}
+
+extern "C" LATENT_API int latent_expert_ffn_workspace_size(const latent_ffn_desc *desc, size_t *bytes) {
+    if (!bytes) return LATENT_ERR_INVALID;
+    const int st = validate(desc, false);
+    if (st) return st;
+    const DecodeArgs a = decode_args(desc);
+    *bytes = layout(desc, a).total;
+    return LATENT_OK;
+}
+
+namespace {
+
+int forward_impl(const latent_ffn_desc *desc, CUstream_st *stream, Marks *marks) {
+    int st = validate(desc, true);
+    if (st) return st;
+    if (desc->n_tokens == 0) return LATENT_OK;
+    const int path = pick_path(desc);
+    if (path == LATENT_PATH_PREFILL) return LATENT_ERR_UNSUPPORTED;
+    DecodeArgs a = decode_args(desc);
+    const Layout L = layout(desc, a);
+    if (!desc->workspace || desc->workspace_bytes < L.total) return LATENT_ERR_WORKSPACE;
+    if (!aligned(desc->workspace, kAlign)) return LATENT_ERR_ALIGN;
+    void *ws = desc->workspace;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+    RouteArgs ra{};
+    ra.ids = desc->ids;
+    ra.R = a.R;
+    ra.E = a.E;
+    ra.top_k = a.k;
+    ra.err = at<uint32_t>(ws, L.err);
+    ra.sem = at<uint32_t>(ws, L.sem);
+    ra.n_sem = L.n_sem;
+    ra.counts = at<int32_t>(ws, L.counts);
+    ra.offsets = at<int32_t>(ws, L.offsets);
+    ra.active = at<int32_t>(ws, L.active);
+    ra.n_active = at<int32_t>(ws, L.n_active);
+    ra.order = at<int32_t>(ws, L.order);
+    ra.pos = at<int32_t>(ws, L.pos);
+    ra.block_counts = at<int32_t>(ws, L.block_counts);
+    if (marks) marks->mark(s);
+    if ((st = cuda_status(launch_route(ra, s)))) return st;
+    if (marks) marks->mark(s);
+
+    a.rt.counts = ra.counts;
+    a.rt.offsets = ra.offsets;
+    a.rt.active = ra.active;
+    a.rt.n_active = ra.n_active;
+    a.rt.order = ra.order;
+    a.rt.pos = ra.pos;
+    a.rt.sem = ra.sem;
+    a.rt.err = ra.err;
+    float *f = at<float>(ws, L.scratch);
+    const size_t R = (size_t)a.R, r = (size_t)a.r;
+    a.part1 = f;  f += (size_t)a.ks1 * R * 2 * r;
+    a.t = f;      f += R * 2 * r;
+    a.h = f;      f += R * (size_t)a.f;
+    a.part2 = f;  f += (size_t)a.ks2 * R * r;
+    a.s = f;      f += R * r;
+    a.y = f;
+    return cuda_status(launch_decode(a, s, marks));
+}
+
+}  // namespace
+
+extern "C" LATENT_API int latent_expert_ffn_forward(const latent_ffn_desc *desc, CUstream_st *stream) {
+    return forward_impl(desc, stream, nullptr);
+}
+
+extern "C" LATENT_API int latent_expert_ffn_forward_timed(const latent_ffn_desc *desc, CUstream_st *stream,
+                                                          CUevent_st *const *events, int n_events) {
+    if (n_events < 0 || (n_events > 0 && !events)) return LATENT_ERR_INVALID;
+    Marks m;
+    m.ev = reinterpret_cast<cudaEvent_t const *>(events);
+    m.n = n_events;
+    return forward_impl(desc, stream, &m);
+}
+
+extern "C" LATENT_API int latent_expert_ffn_check(const latent_ffn_desc *desc, CUstream_st *stream) {
+    if (!desc || !desc->workspace) return LATENT_ERR_INVALID;
+    uint32_t err = 0;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaStreamSynchronize(s) != cudaSuccess) return LATENT_ERR_CUDA;
+    if (desc->n_tokens == 0) return LATENT_OK;
+    if (cudaMemcpy(&err, desc->workspace, sizeof(err), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return LATENT_ERR_CUDA;
+    if (err & kErrExpertId) return LATENT_ERR_EXPERT_ID;
+    if (err & kErrTimeout) return LATENT_ERR_TIMEOUT;
+    return LATENT_OK;
+}
+
+extern "C" LATENT_API int latent_dequantize(const latent_qmatrix *m, int32_t expert, float *out, CUstream_st *stream) {
+    if (!m || !out || !m->codes || !m->scales || expert < 0) return LATENT_ERR_INVALID;
+    if (m->rows < 1 || m->cols < 32 || m->cols % 32) return LATENT_ERR_SHAPE;
+    if (!aligned(m->codes, 16) || !aligned(m->scales, 2) || !aligned(out, 16)) return LATENT_ERR_ALIGN;
+    const bool any = m->i8_mask || m->i8_base || m->i8_hi;
+    if (any && !(m->i8_mask && m->i8_base && m->i8_hi)) return LATENT_ERR_INVALID;
+    return cuda_status(launch_dequant(*m, expert, out, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+extern "C" LATENT_API int latent_silu(const float *x, float *y, int64_t n, CUstream_st *stream) {
+    if (n < 0 || (n > 0 && (!x || !y))) return LATENT_ERR_INVALID;
+    return cuda_status(launch_silu(x, y, n, reinterpret_cast<cudaStream_t>(stream)));
+}

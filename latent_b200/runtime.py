@@ -1,0 +1,286 @@
+"""B200 runtime with the API of LATENT's CPU runtime (loader/latent_runtime.py:13-73).
+
+Same names and argument meaning as the reference -- ``FactorPair``,
+``load_pair``, ``project``, ``silu``, ``swiglu_expert``,
+``dense_swiglu_expert`` -- plus the batched routed op ``moe_expert_ffn``
+(GGML_OP_LATENT_EXPERT_FFN semantics).  Inputs may be numpy arrays (results
+come back as numpy, like the reference) or torch tensors (results stay on
+the device).  Factors stay packed on the device; nothing is dequantized to a
+dense fp32 matrix on the fused path.  Every compute call goes through the
+CUDA library; there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import Dict, Mapping, Optional, Tuple
+
+import numpy as np
+import torch
+
+from . import _lib
+from .format import ExpertSet, GroupedFactor, from_npz
+
+__all__ = ["FactorPair", "load_pair", "project", "silu", "swiglu_expert", "dense_swiglu_expert",
+           "moe_expert_ffn", "ExpertFFN", "workspace_bytes", "dequantize"]
+
+_X_TYPES = {torch.float32: _lib.TYPE_F32, torch.float16: _lib.TYPE_F16, torch.bfloat16: _lib.TYPE_BF16}
+_W_TYPES = {torch.float32: _lib.TYPE_F32, torch.float16: _lib.TYPE_F16}
+
+
+def _device(device=None) -> torch.device:
+    if device is None:
+        if not torch.cuda.is_available():
+            raise RuntimeError("latent_b200 needs a CUDA device (no CPU fallback)")
+        return torch.device("cuda", torch.cuda.current_device())
+    return torch.device(device)
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+@dataclass
+class FactorPair:
+    """A low-rank pair W ~= A @ B kept packed on the device (reference FactorPair, latent_runtime.py:13-16)."""
+
+    a: GroupedFactor
+    b: GroupedFactor
+    _sets: Dict[Tuple[int, int], ExpertSet] = field(default_factory=dict, repr=False, compare=False)
+
+
+def load_pair(arrays: Mapping[str, np.ndarray], name: str, device=None) -> FactorPair:
+    """Reference-NPZ factors ``<name>.{a,b}.*`` -> device pair (latent_runtime.py:19-32).
+
+    NF4 (group 32) is used when present, else INT8 (group 64); a missing
+    factor raises ``KeyError`` like the reference.
+    """
+    dev = _device(device)
+    return FactorPair(from_npz(arrays, name, "a").to(dev), from_npz(arrays, name, "b").to(dev))
+
+
+def dequantize(factor, expert: int = 0) -> torch.Tensor:
+    """Dequantize one factor (GroupedFactor or StackedFactor expert) to fp32 on the device, bit-exact."""
+    from .format import StackedFactor
+    sf = factor if isinstance(factor, StackedFactor) else StackedFactor([factor], factor.lo.device)
+    dev = sf.codes.device
+    out = torch.empty((sf.rows, sf.cols), dtype=torch.float32, device=dev)
+    qm = sf.qmatrix()
+    _lib.check(_lib.lib().latent_dequantize(C.byref(qm), int(expert), out.data_ptr(), _stream_ptr(dev)),
+               "latent_dequantize")
+    return out
+
+
+def _as_device_f32(x, dev) -> Tuple[torch.Tensor, bool]:
+    if isinstance(x, np.ndarray) or not torch.is_tensor(x):
+        return torch.as_tensor(np.asarray(x, dtype=np.float32)).to(dev), True
+    return x.to(device=dev, dtype=torch.float32), False
+
+
+def silu(x):
+    """SiLU elementwise in fp32 on the device (latent_runtime.py:39-45)."""
+    dev = _device(x.device if torch.is_tensor(x) and x.is_cuda else None)
+    xt, host = _as_device_f32(x, dev)
+    xt = xt.contiguous()
+    y = torch.empty_like(xt)
+    _lib.check(_lib.lib().latent_silu(xt.data_ptr(), y.data_ptr(), xt.numel(), _stream_ptr(dev)), "latent_silu")
+    return y.cpu().numpy() if host else y
+
+
+def project(x, pair: FactorPair):
+    """(x @ A) @ B in fp32 (latent_runtime.py:35-36).
+
+    A utility: A and B are dequantized bit-exactly by the CUDA library and
+    multiplied with fp32 GEMMs (TF32 off).  The fused expert path never
+    materialises the factors.
+    """
+    dev = pair.a.lo.device
+    xt, host = _as_device_f32(x, dev)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        y = (xt @ dequantize(pair.a)) @ dequantize(pair.b)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return y.cpu().numpy() if host else y
+
+
+def dense_swiglu_expert(x, gate, up, down, weight: float = 1.0, weight_before_down: bool = False):
+    """Dense SwiGLU reference on the device (latent_runtime.py:62-73); the dense-fallback expert form."""
+    dev = _device(gate.device if torch.is_tensor(gate) and gate.is_cuda else None)
+    xt, host = _as_device_f32(x, dev)
+    g, u, dn = (_as_device_f32(m, dev)[0] for m in (gate, up, down))
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        h = silu(xt @ g) * (xt @ u)
+        if weight_before_down:
+            h = h * torch.as_tensor(weight, dtype=torch.float32, device=dev)
+        y = h @ dn
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return y.cpu().numpy() if host else y
+
+
+def _make_desc(experts: ExpertSet, T: int, k: int, x_type: int, w_type: int, flags: int, path: int) -> _lib.FfnDesc:
+    d = _lib.FfnDesc()
+    d.n_expert, d.n_embd, d.n_ff, d.rank = experts.n_expert, experts.n_embd, experts.n_ff, experts.rank
+    d.n_tokens, d.top_k = T, k
+    d.x_type, d.w_type, d.flags, d.path = x_type, w_type, flags, path
+    for kind in ("gate_a", "gate_b", "up_a", "up_b", "down_a", "down_b"):
+        setattr(d, kind, experts[kind].qmatrix())
+    return d
+
+
+_PATHS = {None: _lib.PATH_AUTO, "auto": _lib.PATH_AUTO, "decode": _lib.PATH_DECODE, "prefill": _lib.PATH_PREFILL}
+
+
+def workspace_bytes(experts: ExpertSet, n_tokens: int, top_k: int, weight_before_down: bool = False,
+                    out_per_slot: bool = False, path: Optional[str] = None,
+                    x_dtype=torch.bfloat16, w_dtype=torch.float32) -> int:
+    """Workspace the fused op needs for a batch of this shape (latent_expert_ffn_workspace_size)."""
+    flags = (_lib.FLAG_WEIGHT_BEFORE_DOWN if weight_before_down else 0) | (_lib.FLAG_OUT_PER_SLOT if out_per_slot else 0)
+    d = _make_desc(experts, n_tokens, top_k, _X_TYPES[x_dtype], _W_TYPES[w_dtype], flags, _PATHS[path])
+    n = C.c_size_t(0)
+    _lib.check(_lib.lib().latent_expert_ffn_workspace_size(C.byref(d), C.byref(n)), "workspace_size")
+    return int(n.value)
+
+
+class ExpertFFN:
+    """The routed latent expert FFN over one ExpertSet (GGML_OP_LATENT_EXPERT_FFN).
+
+    Calling it runs routing, the fused expert chain and the top-k combine on
+    the current CUDA stream.  The workspace is allocated once per shape by
+    this (host-side) object through torch and reused; the CUDA library
+    itself allocates nothing.
+    """
+
+    def __init__(self, experts: ExpertSet, path: Optional[str] = None):
+        self.experts = experts
+        self.path = _PATHS[path]
+        self._ws: Optional[torch.Tensor] = None
+        self._last_desc: Optional[_lib.FfnDesc] = None
+
+    def _workspace(self, nbytes: int) -> torch.Tensor:
+        if self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.experts.device)
+        return self._ws
+
+    def describe(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, out: torch.Tensor,
+                 weight_before_down: bool = False, out_per_slot: bool = False) -> _lib.FfnDesc:
+        """Validated descriptor for these device tensors (with workspace bound)."""
+        ex = self.experts
+        if x.dim() != 2 or x.shape[1] != ex.n_embd:
+            raise ValueError(f"x must be [T, {ex.n_embd}], got {tuple(x.shape)}")
+        T = x.shape[0]
+        if ids.dim() != 2 or ids.shape[0] != T or ids.dtype != torch.int32:
+            raise ValueError("ids must be int32 [T, k]")
+        k = ids.shape[1]
+        if weights.shape != ids.shape or weights.dtype not in _W_TYPES:
+            raise ValueError("weights must be float32/float16 [T, k]")
+        if x.dtype not in _X_TYPES:
+            raise ValueError(f"x dtype {x.dtype} unsupported")
+        for t in (x, ids, weights, out):
+            if t.device != ex.device or not t.is_contiguous():
+                raise ValueError("x, ids, weights and out must be contiguous tensors on the experts' device")
+        flags = (_lib.FLAG_WEIGHT_BEFORE_DOWN if weight_before_down else 0) | \
+                (_lib.FLAG_OUT_PER_SLOT if out_per_slot else 0)
+        d = _make_desc(ex, T, k, _X_TYPES[x.dtype], _W_TYPES[weights.dtype], flags, self.path)
+        n = C.c_size_t(0)
+        _lib.check(_lib.lib().latent_expert_ffn_workspace_size(C.byref(d), C.byref(n)), "workspace_size")
+        ws = self._workspace(int(n.value))
+        d.x, d.ids, d.weights, d.out = x.data_ptr(), ids.data_ptr(), weights.data_ptr(), out.data_ptr()
+        d.workspace, d.workspace_bytes = ws.data_ptr(), ws.numel()
+        return d
+
+    def __call__(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, weight_before_down: bool = False,
+                 out_per_slot: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        T, k = ids.shape
+        shape = (T, k, self.experts.n_embd) if out_per_slot else (T, self.experts.n_embd)
+        if out is None:
+            out = torch.empty(shape, dtype=torch.float32, device=self.experts.device)
+        elif tuple(out.shape) != shape or out.dtype != torch.float32:
+            raise ValueError(f"out must be float32 {shape}")
+        d = self.describe(x, ids, weights, out, weight_before_down, out_per_slot)
+        self._last_desc = d
+        _lib.check(_lib.lib().latent_expert_ffn_forward(C.byref(d), _stream_ptr(self.experts.device)),
+                   "latent_expert_ffn_forward")
+        return out
+
+    def call_timed(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, events,
+                   weight_before_down: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Like ``__call__``; records ``events`` (recorded torch.cuda.Event objects) around every kernel."""
+        T, k = ids.shape
+        if out is None:
+            out = torch.empty((T, self.experts.n_embd), dtype=torch.float32, device=self.experts.device)
+        d = self.describe(x, ids, weights, out, weight_before_down, False)
+        self._last_desc = d
+        handles = (C.c_void_p * len(events))(*[ev.cuda_event for ev in events])
+        _lib.check(_lib.lib().latent_expert_ffn_forward_timed(
+            C.byref(d), _stream_ptr(self.experts.device), handles, len(events)), "latent_expert_ffn_forward_timed")
+        return out
+
+    def check(self) -> None:
+        """Synchronises and raises if the last call routed an expert id >= n_expert."""
+        if self._last_desc is not None:
+            _lib.check(_lib.lib().latent_expert_ffn_check(C.byref(self._last_desc),
+                                                          _stream_ptr(self.experts.device)), "device check")
+
+
+def _to_dev(a, dev, dtype=None):
+    if torch.is_tensor(a):
+        return a.to(device=dev, dtype=dtype if dtype is not None else a.dtype).contiguous()
+    arr = np.asarray(a)
+    t = torch.from_numpy(np.ascontiguousarray(arr))
+    return t.to(device=dev, dtype=dtype if dtype is not None else t.dtype).contiguous()
+
+
+_OPS: Dict[int, ExpertFFN] = {}
+
+
+def moe_expert_ffn(x, ids, weights, experts: ExpertSet, weight_before_down: bool = False,
+                   out_per_slot: bool = False, path: Optional[str] = None):
+    """Batched routed expert FFN: out[t] = sum_j w[t,j] * swiglu_expert_{ids[t,j]}(x[t]).
+
+    ``ids`` < 0 skip a slot.  numpy inputs give a numpy result.
+    """
+    host = not torch.is_tensor(x)
+    dev = experts.device
+    xt = _to_dev(x, dev, torch.float32 if host and np.asarray(x).dtype == np.float64 else None)
+    it = _to_dev(ids, dev, torch.int32)
+    wt = _to_dev(weights, dev, torch.float32 if (host or weights.dtype not in _W_TYPES) else None)
+    key = id(experts) * 4 + _PATHS[path]
+    op = _OPS.get(key)
+    if op is None or op.experts is not experts:
+        op = _OPS[key] = ExpertFFN(experts, path)
+    y = op(xt, it, wt, weight_before_down, out_per_slot)
+    return y.cpu().numpy() if host else y
+
+
+def swiglu_expert(x, gate: FactorPair, up: FactorPair, down: FactorPair, weight=1.0,
+                  weight_before_down: bool = False):
+    """SwiGLU expert over packed factor pairs (latent_runtime.py:48-59).
+
+    Returns silu((x@A_g)@B_g) * ((x@A_u)@B_u) [* weight] @ A_d @ B_d; the weight
+    only enters when ``weight_before_down`` (the caller applies it otherwise).
+    """
+    key = (id(up), id(down))
+    es = gate._sets.get(key)
+    if es is None:
+        es = gate._sets[key] = ExpertSet([{"gate_a": gate.a, "gate_b": gate.b, "up_a": up.a, "up_b": up.b,
+                                           "down_a": down.a, "down_b": down.b}], device=gate.a.lo.device)
+    host = not torch.is_tensor(x)
+    xt = _to_dev(x, es.device, torch.float32 if host else None)
+    one_d = xt.dim() == 1
+    if one_d:
+        xt = xt[None, :]
+    T = xt.shape[0]
+    ids = torch.zeros((T, 1), dtype=torch.int32, device=es.device)
+    w = torch.as_tensor(weight, dtype=torch.float32, device=es.device) if weight_before_down else \
+        torch.ones((), dtype=torch.float32, device=es.device)
+    w = w.reshape(-1, 1).expand(T, 1).contiguous()
+    y = moe_expert_ffn(xt, ids, w, es, weight_before_down=weight_before_down)
+    if one_d:
+        y = y[0]
+    return y.cpu().numpy() if host else y

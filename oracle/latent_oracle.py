@@ -33,6 +33,7 @@ __all__ = [
     "group_snr",
     "mixed_encode",
     "mixed_decode",
+    "decode_grouped",
     "silu",
     "project",
     "swiglu_expert",
@@ -166,6 +167,31 @@ def mixed_decode(enc: Mapping[str, np.ndarray], group: int = 32) -> np.ndarray:
         full[is_i8] = i8[is_i8]
         out = full.ravel()[:n]
     return out.reshape(shape)
+
+
+def decode_grouped(lo: np.ndarray, hi: np.ndarray, scales: np.ndarray, is_int8: np.ndarray,
+                   rows: int, cols: int) -> np.ndarray:
+    """Decode the row-aligned group layout the CUDA library consumes.
+
+    ``lo``/``hi`` are [groups, 16] packed nibbles, ``scales`` fp16 (or its bit
+    pattern) [groups], ``is_int8`` bool [groups].  NF4 groups go through the
+    reference NF4 decoder (loader/latent_loader.py:133-145) with their codes
+    in ``lo``; INT8 groups through the reference INT8 decoder (:161-170) with
+    q = int8(hi << 4 | lo).
+    """
+    lo = np.asarray(lo, dtype=np.uint8).reshape(-1, 16)
+    hi = np.asarray(hi, dtype=np.uint8).reshape(-1, 16)
+    sc = np.asarray(scales).reshape(-1)
+    sc = sc.view(np.float16) if sc.dtype != np.float16 else sc
+    is_i8 = np.asarray(is_int8, dtype=bool).reshape(-1)
+    n_groups = lo.shape[0]
+    out = nf4_decode(lo.ravel(), sc, (n_groups * 32,), 32).reshape(n_groups, 32)
+    if is_i8.any():
+        def nib(b):
+            return np.stack([b & 0xF, b >> 4], axis=-1).reshape(b.shape[0], 32)
+        q = ((nib(hi[is_i8]) << 4) | nib(lo[is_i8])).astype(np.uint8).view(np.int8)
+        out[is_i8] = int8_decode(q.ravel(), sc[is_i8], (int(is_i8.sum()) * 32,), 32).reshape(-1, 32)
+    return out.reshape(rows, cols)
 
 
 def silu(x: np.ndarray) -> np.ndarray:

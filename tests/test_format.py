@@ -1,0 +1,121 @@
+"""Host-side packing and quantization against the oracle (CPU only)."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import golden
+from latent_b200 import format as F
+from latent_b200.quant import quantize_factor
+
+
+def _decode(gf: F.GroupedFactor) -> np.ndarray:
+    return O.decode_grouped(gf.lo.cpu().numpy(), gf.hi.cpu().numpy(), gf.scales.cpu().numpy().view(np.uint16),
+                            gf.is_int8.cpu().numpy(), gf.rows, gf.cols)
+
+
+def _bits(a):
+    return np.asarray(a, np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize("variant", ["nf4", "int8"])
+def test_reference_npz_factors_decode_bit_exact(variant):
+    z = golden("runtime")
+    arrays = {k.split("/", 1)[1]: z[k] for k in z.files if k.startswith(variant + "/")}
+    for name in ("gate", "up", "down"):
+        for side in ("a", "b"):
+            gf = F.from_npz(arrays, name, side)
+            ref = O.factor_from_npz(arrays, name, side)
+            assert np.array_equal(_bits(_decode(gf)), _bits(ref)), (variant, name, side)
+            assert bool(gf.is_int8.all()) == (variant == "int8")
+
+
+def test_mixed_golden_decodes_bit_exact():
+    z = golden("mixed")
+    gf = F.from_mixed(z["nf4"], z["scales"], z["is_int8"], z["int8"], z["values"].shape)
+    assert np.array_equal(_bits(_decode(gf)), _bits(z["decoded"]))
+
+
+def test_missing_factor_raises_keyerror():
+    z = golden("runtime")
+    arrays = {k.split("/", 1)[1]: z[k] for k in z.files if k.startswith("nf4/") and not k.endswith(".nf4")}
+    with pytest.raises(KeyError):
+        F.from_npz(arrays, "gate", "a")
+
+
+def test_unaligned_columns_rejected():
+    packed, scales, shape = O.nf4_encode(np.ones((4, 12), np.float32))
+    with pytest.raises(ValueError):
+        F.from_nf4(packed, scales, shape)
+
+
+@pytest.mark.parametrize("snr_db", [None, 20.0, 35.0])
+def test_quantizer_matches_oracle_encoders(snr_db):
+    rng = np.random.default_rng(3)
+    v = rng.standard_normal((48, 96)).astype(np.float32)
+    v[:, 7] *= 30.0            # outlier column -> low-SNR groups
+    v[5] = 0.0                 # all-zero groups
+    v[6, :30] = O.NF4_LEVELS[:-1].tolist() + O.NF4_LEVELS[1:].tolist()  # exact levels in a group
+    v[6, 31] = 1.0
+    gf = quantize_factor(torch.from_numpy(v), snr_db)
+    if snr_db is None:
+        packed, scales, _ = O.nf4_encode(v)
+        assert np.array_equal(gf.lo.numpy().ravel(), packed)
+        assert np.array_equal(gf.scales.numpy().ravel().view(np.uint16), scales.view(np.uint16))
+        assert not gf.is_int8.any()
+    else:
+        enc = O.mixed_encode(v, snr_db=snr_db)
+        assert np.array_equal(gf.is_int8.numpy().ravel(), enc["is_int8"])
+        assert enc["is_int8"].any()
+        assert np.array_equal(gf.scales.numpy().ravel().view(np.uint16), enc["scales"].view(np.uint16))
+        assert np.array_equal(_bits(_decode(gf)), _bits(O.mixed_decode(enc)))
+
+
+def test_quantizer_tie_midpoints_pick_lowest_code():
+    lv = O.NF4_LEVELS
+    mids = ((lv[:-1] + lv[1:]) / 2).astype(np.float32)
+    v = np.zeros((1, 32), np.float32)
+    v[0, 0] = 1.0
+    v[0, 1:16] = mids
+    packed, _, _ = O.nf4_encode(v)
+    gf = quantize_factor(torch.from_numpy(v), None)
+    assert np.array_equal(gf.lo.numpy().ravel(), packed)
+
+
+def test_padding_and_stacking_roundtrip():
+    rng = np.random.default_rng(4)
+    fs = []
+    for e in range(3):
+        v = rng.standard_normal((40, 64)).astype(np.float32)
+        v[:, 3] *= 50
+        fs.append(quantize_factor(torch.from_numpy(v), 20.0))
+    padded = [f.padded(40, 128) for f in fs]
+    for f, p in zip(fs, padded):
+        dp = _decode(p)
+        assert np.array_equal(_bits(dp[:, :64]), _bits(_decode(f)))
+        assert not dp[:, 64:].any()
+    st = F.StackedFactor(padded, "cpu")
+    assert st.n_int8 == sum(f.n_int8 for f in fs) > 0
+    for e, p in enumerate(padded):
+        back = st.expert(e)
+        assert np.array_equal(_bits(_decode(back)), _bits(_decode(p)))
+    # the mask/base tables describe the compact sidecar
+    m = st.i8_mask.numpy().view(np.uint32)
+    base = st.i8_base.numpy()
+    counts = np.array([[bin(int(w)).count("1") for w in row] for row in m])
+    assert np.array_equal(base.ravel(), np.concatenate([[0], np.cumsum(counts.ravel())[:-1]]))
+
+
+def test_expert_set_pads_rank_and_counts_bytes():
+    rng = np.random.default_rng(5)
+    d, f, r = 64, 96, 32
+    ex = {}
+    for name, (m, n) in (("gate", (d, f)), ("up", (d, f)), ("down", (f, d))):
+        ex[f"{name}_a"] = quantize_factor(torch.from_numpy(rng.standard_normal((m, r)).astype(np.float32)), None)
+        ex[f"{name}_b"] = quantize_factor(torch.from_numpy(rng.standard_normal((r, n)).astype(np.float32)), None)
+    es = F.ExpertSet([ex, ex], device="cpu", rank=64)
+    assert es.rank == 64 and es["gate_a"].cols == 64 and es["down_b"].rows == 64
+    per = 3 * (d * 64 + 64 * f) + 3 * 0  # elements per expert... 3 A (rows*64) + 3 B (64*cols)
+    elems = 2 * d * 64 + f * 64 + 2 * 64 * f + 64 * d
+    assert es.factor_bytes([0]) == elems // 2 + elems // 32 * 2

@@ -1,0 +1,67 @@
+"""The decode path at the benchmark's full size (config 1: 64 experts,
+d=2048, f=1408, r=256, top-6, 32 tokens, bf16 activations): a sample of tokens
+against the oracle, plus size-independent properties over the whole batch."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from gpu_helpers import decode, rel
+from latent_b200 import ExpertFFN, synth
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def c1(cuda):
+    cfg = synth.CONFIGS[1]
+    es = synth.make_expert_set(cfg, device="cuda")
+    x, ids, w = synth.make_batch(cfg, "cuda")
+    return cfg, es, x, ids, w
+
+
+def _oracle_experts(es, experts):
+    out = {}
+    for e in experts:
+        out[e] = tuple((decode(es[f"{n}_a"].expert(e)), decode(es[f"{n}_b"].expert(e))) for n in ("gate", "up", "down"))
+    return out
+
+
+def test_token_sample_matches_oracle(c1):
+    cfg, es, x, ids, w = c1
+    y = ExpertFFN(es, path="decode")(x, ids, w).cpu().numpy()
+    sample = [0, 13, 31]
+    ids_s = ids[sample].cpu().numpy()
+    touched = sorted(set(ids_s.ravel().tolist()))
+    ex = _oracle_experts(es, touched)
+    table = [ex.get(e) for e in range(cfg.n_expert)]
+    ref = O.moe_forward(x[sample].float().cpu().numpy(), ids_s, w[sample].cpu().numpy(), table)
+    assert rel(ref, y[sample]) <= TOL
+
+
+def test_weight_scaling_is_exact(c1):
+    cfg, es, x, ids, w = c1
+    op = ExpertFFN(es, path="decode")
+    y1 = op(x, ids, w).clone()
+    y2 = op(x, ids, w * 2.0)
+    assert torch.equal(y1 * 2.0, y2)
+
+
+def test_token_permutation_is_bitwise_equivariant(c1):
+    cfg, es, x, ids, w = c1
+    op = ExpertFFN(es, path="decode")
+    y = op(x, ids, w).clone()
+    perm = torch.randperm(x.shape[0], generator=torch.Generator().manual_seed(9)).to(x.device)
+    yp = op(x[perm].contiguous(), ids[perm].contiguous(), w[perm].contiguous())
+    assert torch.equal(y[perm], yp)
+
+
+def test_per_slot_rows_sum_to_combined(c1):
+    cfg, es, x, ids, w = c1
+    op = ExpertFFN(es, path="decode")
+    y = op(x, ids, w).clone()
+    ps = op(x, ids, w, out_per_slot=True)
+    comb = (ps.double() * w.double()[:, :, None]).sum(dim=1)
+    assert rel(comb.cpu().numpy(), y) <= 1e-6
