@@ -320,6 +320,112 @@ def run_ours(args, world, rank, local):
     return line
 
 
+class _TimedOps:
+    """Wraps the EP ops to record events around the local fused FFN (the dominant kernel chain)."""
+
+    def __init__(self, ops):
+        self.ops = ops
+        self.ev = None
+
+    def dispatch(self, *a):
+        return self.ops.dispatch(*a)
+
+    def local_ffn(self, rx, lids, rw, wbd):
+        if self.ev is not None:
+            self.ev[0].record()
+        y = self.ops.local_ffn(rx, lids, rw, wbd)
+        if self.ev is not None:
+            self.ev[1].record()
+        return y
+
+    def combine(self, *a):
+        return self.ops.combine(*a)
+
+
+def run_ours_ep(args, world, rank, local):
+    """Expert-parallel step on `world` GPUs: experts sharded contiguously, a full config batch per rank
+    (weak scaling), NCCL all-to-all dispatch and return."""
+    from latent_b200 import ExpertSet, synth
+    from latent_b200.ep import CudaEPOps, ExpertParallelFFN
+    dev = torch.device("cuda", local)
+    cfg = synth.CONFIGS[args.config]
+    e_local = cfg.n_expert // world
+    t0 = time.perf_counter()
+    facs = synth.make_expert_factors(cfg, dev, experts=range(rank * e_local, (rank + 1) * e_local))
+    es = ExpertSet(facs, device=dev, rank=cfg.rank)
+    x, ids, w = synth.make_batch(cfg, dev, seed_offset=rank)
+    gen_s = time.perf_counter() - t0
+    ops = _TimedOps(CudaEPOps(es, cfg.n_expert))
+    ep = ExpertParallelFFN(cfg.n_expert, ops)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        ep(x, ids, w)
+    torch.cuda.synchronize()
+    steps = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ffn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    recv_rows = []
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    for k in range(args.steps):
+        flush.zero_()
+        ops.ev = ffn[k]
+        steps[k][0].record()
+        ep(x, ids, w)
+        steps[k][1].record()
+        recv_rows.append(sum(ep.last_counts[1]))
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ops.ev = None
+    ms_local = statistics.mean(a.elapsed_time(b) for a, b in steps)
+    ffn_ms = statistics.mean(a.elapsed_time(b) for a, b in ffn)
+    ms = allreduce_max(ms_local, world)
+    routed = int((ids >= 0).sum())
+    routed_all = allreduce_sum(float(routed), world)
+    # every local expert receives rows at this batch size: the local FFN streams all of them
+    local_bytes = es.factor_bytes(range(e_local))
+    ach = local_bytes / (ffn_ms * 1e-3) / 1e9
+    pk = peaks()
+    # e2e with pinned host buffers
+    hx, hids, hw = x.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory()
+    hout = torch.empty((x.shape[0], cfg.n_embd), dtype=torch.float32).pin_memory()
+    dx, dids, dw = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(w)
+    e2e = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for k in range(args.warmup + args.steps):
+        flush.zero_()
+        if k >= args.warmup:
+            e2e[k - args.warmup][0].record()
+        dx.copy_(hx, non_blocking=True)
+        dids.copy_(hids, non_blocking=True)
+        dw.copy_(hw, non_blocking=True)
+        out = ep(dx, dids, dw)
+        hout.copy_(out, non_blocking=True)
+        if k >= args.warmup:
+            e2e[k - args.warmup][1].record()
+    torch.cuda.synchronize()
+    e2e_ms = allreduce_max(statistics.mean(a.elapsed_time(b) for a, b in e2e), world)
+    R = ids.numel()
+    return {
+        "metric": METRIC, "value": routed_all / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE recipe)",
+        "config": config_json(cfg, ids, world, f"expert-parallel ep{world} (NCCL all-to-all)"),
+        "roofline": {"bound": "hbm", "kernel": "local fused expert FFN (rank 0)", "achieved": ach,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "traffic": None,
+                     "algorithmic_bytes": local_bytes, "mean_ms": ffn_ms, "peak_source": pk["source"]},
+        "e2e": {"value": routed_all / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(hx.numel() * hx.element_size() + hids.numel() * 4 + hw.numel() * 4),
+                "d2h_bytes_per_step": int(hout.numel() * 4)},
+        "gpu_launches": args.steps * ((1 if R <= 4096 else 3) + 1 + 6 + 1),
+        "recv_rows_rank0": statistics.mean(recv_rows),
+        "clocks": clk,
+        "gen_s": gen_s,
+    }
+
+
 def run_reference(args, world, rank, local):
     if rank != 0:
         return None
@@ -341,7 +447,12 @@ def main() -> int:
     args = parse_args()
     world, rank, local = dist_setup(args.gpus)
     try:
-        line = run_reference(args, world, rank, local) if args.impl == "reference" else run_ours(args, world, rank, local)
+        if args.impl == "reference":
+            line = run_reference(args, world, rank, local)
+        elif world > 1:
+            line = run_ours_ep(args, world, rank, local)
+        else:
+            line = run_ours(args, world, rank, local)
         if rank == 0 and line is not None:
             print(json.dumps(line), flush=True)
     finally:

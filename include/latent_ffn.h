@@ -134,6 +134,37 @@ typedef struct latent_ffn_desc {
     size_t workspace_bytes;
 } latent_ffn_desc;
 
+/* Expert-parallel dispatch/combine around an NCCL all-to-all (no counterpart
+ * in the reference, which has no multi-GPU code).  dispatch routes the
+ * batch by global expert id and packs one row per routed slot in expert
+ * order -- destination-rank order when experts are contiguous per rank;
+ * combine folds the expert outputs that came back (same row order) into
+ * out[T][d] with the router weights, in slot order. */
+typedef struct latent_ep_desc {
+    int32_t n_expert;       /* global E */
+    int32_t n_embd;         /* d (multiple of 32) */
+    int32_t n_tokens;       /* T */
+    int32_t top_k;          /* k */
+    int32_t x_type;         /* latent_type of x and send_x */
+    int32_t w_type;         /* latent_type of weights */
+    uint32_t flags;         /* LATENT_FLAG_WEIGHT_BEFORE_DOWN: combine sums without weights */
+    const void *x;          /* [T][d] */
+    const int32_t *ids;     /* [T][k] */
+    const void *weights;    /* [T][k] */
+    void *send_x;           /* out: [T*k][d] rows in expert order (first sum(expert_counts) valid) */
+    int32_t *send_expert;   /* out: [T*k] global expert id of each row */
+    float *send_weight;     /* out: [T*k] router weight of each row */
+    int32_t *expert_counts; /* out: [E] rows per expert */
+    const float *y_back;    /* in (combine): [T*k][d] expert outputs in send order */
+    float *out;             /* out (combine): [T][d] */
+    void *workspace;        /* kept between dispatch and combine */
+    size_t workspace_bytes;
+} latent_ep_desc;
+
+LATENT_API int latent_ep_workspace_size(const latent_ep_desc *desc, size_t *bytes);
+LATENT_API int latent_ep_dispatch(const latent_ep_desc *desc, struct CUstream_st *stream);
+LATENT_API int latent_ep_combine(const latent_ep_desc *desc, struct CUstream_st *stream);
+
 /* ABI version of the loaded library (LATENT_ABI_VERSION). */
 LATENT_API int latent_abi_version(void);
 

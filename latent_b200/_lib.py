@@ -69,7 +69,33 @@ class FfnDesc(C.Structure):
     ]
 
 
+class EpDesc(C.Structure):
+    _fields_ = [
+        ("n_expert", C.c_int32),
+        ("n_embd", C.c_int32),
+        ("n_tokens", C.c_int32),
+        ("top_k", C.c_int32),
+        ("x_type", C.c_int32),
+        ("w_type", C.c_int32),
+        ("flags", C.c_uint32),
+        ("x", C.c_void_p),
+        ("ids", C.c_void_p),
+        ("weights", C.c_void_p),
+        ("send_x", C.c_void_p),
+        ("send_expert", C.c_void_p),
+        ("send_weight", C.c_void_p),
+        ("expert_counts", C.c_void_p),
+        ("y_back", C.c_void_p),
+        ("out", C.c_void_p),
+        ("workspace", C.c_void_p),
+        ("workspace_bytes", C.c_size_t),
+    ]
+
+
 EXPORTS.update({
+    "latent_ep_workspace_size": (C.c_int, [C.POINTER(EpDesc), C.POINTER(C.c_size_t)]),
+    "latent_ep_dispatch": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
+    "latent_ep_combine": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_abi_version": (C.c_int, []),
     "latent_status_string": (C.c_char_p, [C.c_int]),
     "latent_expert_ffn_workspace_size": (C.c_int, [C.POINTER(FfnDesc), C.POINTER(C.c_size_t)]),

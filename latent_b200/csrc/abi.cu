@@ -252,6 +252,118 @@ extern "C" LATENT_API int latent_expert_ffn_check(const latent_ffn_desc *desc, C
     return LATENT_OK;
 }
 
+namespace {
+
+int ep_validate(const latent_ep_desc *d) {
+    if (!d) return LATENT_ERR_INVALID;
+    if (d->n_expert < 1 || d->n_expert > kMaxExperts) return LATENT_ERR_SHAPE;
+    if (d->n_embd < 32 || d->n_embd % 32 || d->n_tokens < 0 || d->top_k < 1) return LATENT_ERR_SHAPE;
+    if ((int64_t)d->n_tokens * d->top_k > (int64_t)1 << 30) return LATENT_ERR_SHAPE;
+    if (d->x_type != LATENT_TYPE_F32 && d->x_type != LATENT_TYPE_F16 && d->x_type != LATENT_TYPE_BF16)
+        return LATENT_ERR_DTYPE;
+    if (d->w_type != LATENT_TYPE_F32 && d->w_type != LATENT_TYPE_F16) return LATENT_ERR_DTYPE;
+    if (d->flags & ~(uint32_t)LATENT_FLAG_WEIGHT_BEFORE_DOWN) return LATENT_ERR_INVALID;
+    return LATENT_OK;
+}
+
+// Routing-only layout (the prefix of the forward layout, no FFN scratch).
+Layout ep_layout(const latent_ep_desc *d) {
+    latent_ffn_desc f{};
+    f.n_expert = d->n_expert;
+    f.n_embd = d->n_embd;
+    f.n_ff = 32;
+    f.rank = 32;
+    f.n_tokens = d->n_tokens;
+    f.top_k = d->top_k;
+    DecodeArgs a = decode_args(&f);
+    Layout L = layout(&f, a);
+    L.total = L.scratch;
+    return L;
+}
+
+}  // namespace
+
+extern "C" LATENT_API int latent_ep_workspace_size(const latent_ep_desc *desc, size_t *bytes) {
+    if (!bytes) return LATENT_ERR_INVALID;
+    const int st = ep_validate(desc);
+    if (st) return st;
+    *bytes = ep_layout(desc).total;
+    return LATENT_OK;
+}
+
+extern "C" LATENT_API int latent_ep_dispatch(const latent_ep_desc *desc, CUstream_st *stream) {
+    int st = ep_validate(desc);
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (!desc->expert_counts) return LATENT_ERR_INVALID;
+    if (desc->n_tokens == 0)
+        return cuda_status(cudaMemsetAsync(desc->expert_counts, 0, (size_t)desc->n_expert * 4, s));
+    if (!desc->x || !desc->ids || !desc->weights || !desc->send_x || !desc->send_expert || !desc->send_weight)
+        return LATENT_ERR_INVALID;
+    if (!aligned(desc->x, 16) || !aligned(desc->send_x, 16)) return LATENT_ERR_ALIGN;
+    const Layout L = ep_layout(desc);
+    if (!desc->workspace || desc->workspace_bytes < L.total) return LATENT_ERR_WORKSPACE;
+    if (!aligned(desc->workspace, kAlign)) return LATENT_ERR_ALIGN;
+    void *ws = desc->workspace;
+    RouteArgs ra{};
+    ra.ids = desc->ids;
+    ra.R = desc->n_tokens * desc->top_k;
+    ra.E = desc->n_expert;
+    ra.top_k = desc->top_k;
+    ra.err = at<uint32_t>(ws, L.err);
+    ra.sem = at<uint32_t>(ws, L.sem);
+    ra.n_sem = 0;
+    ra.counts = at<int32_t>(ws, L.counts);
+    ra.offsets = at<int32_t>(ws, L.offsets);
+    ra.active = at<int32_t>(ws, L.active);
+    ra.n_active = at<int32_t>(ws, L.n_active);
+    ra.order = at<int32_t>(ws, L.order);
+    ra.pos = at<int32_t>(ws, L.pos);
+    ra.block_counts = at<int32_t>(ws, L.block_counts);
+    if ((st = cuda_status(launch_route(ra, s)))) return st;
+    if ((st = cuda_status(cudaMemcpyAsync(desc->expert_counts, ra.counts, (size_t)desc->n_expert * 4,
+                                          cudaMemcpyDeviceToDevice, s))))
+        return st;
+    EpArgs e{};
+    e.E = desc->n_expert;
+    e.d = desc->n_embd;
+    e.T = desc->n_tokens;
+    e.k = desc->top_k;
+    e.x_type = desc->x_type;
+    e.w_type = desc->w_type;
+    e.x = desc->x;
+    e.ids = desc->ids;
+    e.weights = desc->weights;
+    e.offsets = ra.offsets;
+    e.order = ra.order;
+    e.send_x = desc->send_x;
+    e.send_expert = desc->send_expert;
+    e.send_weight = desc->send_weight;
+    return cuda_status(launch_ep_gather(e, s));
+}
+
+extern "C" LATENT_API int latent_ep_combine(const latent_ep_desc *desc, CUstream_st *stream) {
+    int st = ep_validate(desc);
+    if (st) return st;
+    if (desc->n_tokens == 0) return LATENT_OK;
+    if (!desc->y_back || !desc->out || !desc->weights) return LATENT_ERR_INVALID;
+    if (!aligned(desc->y_back, 16) || !aligned(desc->out, 16)) return LATENT_ERR_ALIGN;
+    const Layout L = ep_layout(desc);
+    if (!desc->workspace || desc->workspace_bytes < L.total) return LATENT_ERR_WORKSPACE;
+    DecodeArgs a{};
+    a.E = desc->n_expert;
+    a.d = desc->n_embd;
+    a.T = desc->n_tokens;
+    a.k = desc->top_k;
+    a.w_type = desc->w_type;
+    a.flags = desc->flags;
+    a.weights = desc->weights;
+    a.out = desc->out;
+    a.y = const_cast<float *>(desc->y_back);
+    a.rt.pos = at<int32_t>(desc->workspace, L.pos);
+    return cuda_status(launch_combine(a, reinterpret_cast<cudaStream_t>(stream)));
+}
+
 extern "C" LATENT_API int latent_dequantize(const latent_qmatrix *m, int32_t expert, float *out, CUstream_st *stream) {
     if (!m || !out || !m->codes || !m->scales || expert < 0) return LATENT_ERR_INVALID;
     if (m->rows < 1 || m->cols < 32 || m->cols % 32) return LATENT_ERR_SHAPE;

@@ -445,6 +445,11 @@ cudaError_t launch_in(const DecodeArgs &a, int ph, cudaStream_t s) {
 void decode_plan(DecodeArgs &a) {
     a.R = a.T * a.k;
     a.nmax = a.E < a.R ? a.E : a.R;
+    if (a.nmax < 1) {  // empty batch: nothing is launched
+        a.kc1 = a.kc2 = 64;
+        a.ks1 = a.ks2 = 1;
+        return;
+    }
     const int lpr = a.r / 16;
     const int step = kWarps * (32 / (lpr > 32 ? 32 : lpr));
     plan_split(a.d, a.nmax, 2, step, a.kc1, a.ks1);
@@ -486,6 +491,17 @@ cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t s, Marks *marks) {
     err = cudaGetLastError();
     m.mark(s);
     return err;
+}
+
+}  // namespace latent
+
+namespace latent {
+
+cudaError_t launch_combine(const DecodeArgs &a, cudaStream_t s) {
+    if (a.T == 0) return cudaSuccess;
+    dim3 grid((a.d / 4 + 255) / 256, a.T);
+    k_combine<<<grid, 256, 0, s>>>(a);
+    return cudaGetLastError();
 }
 
 }  // namespace latent

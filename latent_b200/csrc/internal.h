@@ -83,6 +83,24 @@ void decode_plan(DecodeArgs &a);
 size_t decode_scratch_floats(const DecodeArgs &a);
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t s, Marks *marks);
 
+// Top-k combine of per-routed-row outputs (a.y) into a.out, slot order.
+cudaError_t launch_combine(const DecodeArgs &a, cudaStream_t s);
+
+struct EpArgs {
+    int E, d, T, k;
+    int x_type, w_type;
+    const void *x;
+    const int32_t *ids;
+    const void *weights;
+    const int32_t *offsets;  // routing results (workspace)
+    const int32_t *order;
+    void *send_x;
+    int32_t *send_expert;
+    float *send_weight;
+};
+
+cudaError_t launch_ep_gather(const EpArgs &a, cudaStream_t s);
+
 cudaError_t launch_dequant(const latent_qmatrix &m, int expert, float *out, cudaStream_t s);
 cudaError_t launch_silu(const float *x, float *y, int64_t n, cudaStream_t s);
 

@@ -1,0 +1,134 @@
+"""Expert parallelism: the routed expert FFN sharded over ranks by expert.
+
+Experts are contiguous per rank (rank g owns experts [g*E/G, (g+1)*E/G)).
+One call, on every rank:
+  1. dispatch (CUDA library): route the local batch by global expert id and
+     pack one row per routed slot in expert order = destination-rank order;
+  2. all-to-all of per-destination row counts, one host read of the counts;
+  3. all-to-all of the rows (x in its dtype) and of (expert id, weight);
+  4. the fused latent FFN over the received rows with the local experts
+     (top-1, weight 1 -- or the router weight before the down projection);
+  5. all-to-all of the fp32 expert outputs back to the source ranks;
+  6. combine (CUDA library): out[t] = sum_j w[t,j] * y_(t,j) in slot order.
+Weights never move.  Every byte between GPUs goes through NCCL into local
+HBM; no kernel reads peer memory.  The reference has no multi-GPU code.
+
+The per-rank compute steps are behind a small ``ops`` interface so that the
+collective bookkeeping can be exercised on CPU ranks (gloo) with a CPU test
+double; the product ops are ``CudaEPOps``.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .format import ExpertSet
+from .runtime import ExpertFFN, _W_TYPES, _X_TYPES, _stream_ptr
+
+
+@dataclass
+class Packed:
+    send_x: torch.Tensor        # [T*k, d] rows in expert order
+    send_expert: torch.Tensor   # [T*k] int32 global expert id
+    send_weight: torch.Tensor   # [T*k] float32
+    expert_counts: torch.Tensor  # [E] int32
+    state: object = None         # whatever combine needs
+
+
+class CudaEPOps:
+    """Dispatch / local FFN / combine through the CUDA library."""
+
+    def __init__(self, local_experts: ExpertSet, n_expert: int, path: Optional[str] = "decode"):
+        self.local = local_experts
+        self.n_expert = n_expert
+        self.ffn = ExpertFFN(local_experts, path=path)
+        self._ws: Optional[torch.Tensor] = None
+
+    def _desc(self, x, ids, weights, wbd: bool) -> _lib.EpDesc:
+        d = _lib.EpDesc()
+        d.n_expert, d.n_embd = self.n_expert, x.shape[1]
+        d.n_tokens, d.top_k = ids.shape
+        d.x_type, d.w_type = _X_TYPES[x.dtype], _W_TYPES[weights.dtype]
+        d.flags = _lib.FLAG_WEIGHT_BEFORE_DOWN if wbd else 0
+        d.x, d.ids, d.weights = x.data_ptr(), ids.data_ptr(), weights.data_ptr()
+        n = C.c_size_t()
+        _lib.check(_lib.lib().latent_ep_workspace_size(C.byref(d), C.byref(n)), "latent_ep_workspace_size")
+        if self._ws is None or self._ws.numel() < n.value:
+            self._ws = torch.empty(max(int(n.value), 256), dtype=torch.uint8, device=x.device)
+        d.workspace, d.workspace_bytes = self._ws.data_ptr(), self._ws.numel()
+        return d
+
+    def dispatch(self, x, ids, weights, wbd: bool) -> Packed:
+        T, k = ids.shape
+        dev = x.device
+        p = Packed(torch.empty((max(T * k, 1), x.shape[1]), dtype=x.dtype, device=dev),
+                   torch.empty(max(T * k, 1), dtype=torch.int32, device=dev),
+                   torch.empty(max(T * k, 1), dtype=torch.float32, device=dev),
+                   torch.empty(self.n_expert, dtype=torch.int32, device=dev))
+        d = self._desc(x, ids, weights, wbd)
+        d.send_x, d.send_expert, d.send_weight = p.send_x.data_ptr(), p.send_expert.data_ptr(), p.send_weight.data_ptr()
+        d.expert_counts = p.expert_counts.data_ptr()
+        _lib.check(_lib.lib().latent_ep_dispatch(C.byref(d), _stream_ptr(dev)), "latent_ep_dispatch")
+        p.state = (x, ids, weights, wbd)
+        return p
+
+    def local_ffn(self, rx, local_ids, rw, wbd: bool) -> torch.Tensor:
+        if rx.shape[0] == 0:
+            return torch.empty((0, rx.shape[1]), dtype=torch.float32, device=rx.device)
+        return self.ffn(rx, local_ids, rw, weight_before_down=wbd)
+
+    def combine(self, p: Packed, y_back: torch.Tensor) -> torch.Tensor:
+        x, ids, weights, wbd = p.state
+        out = torch.empty((ids.shape[0], x.shape[1]), dtype=torch.float32, device=x.device)
+        d = self._desc(x, ids, weights, wbd)
+        d.y_back, d.out = y_back.data_ptr(), out.data_ptr()
+        _lib.check(_lib.lib().latent_ep_combine(C.byref(d), _stream_ptr(x.device)), "latent_ep_combine")
+        return out
+
+
+class ExpertParallelFFN:
+    """Routed expert FFN with experts sharded over the ranks of ``group``."""
+
+    def __init__(self, n_expert: int, ops, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if n_expert % self.world:
+            raise ValueError(f"{n_expert} experts do not split evenly over {self.world} ranks")
+        self.n_expert = n_expert
+        self.e_local = n_expert // self.world
+        self.base = self.rank * self.e_local
+        self.ops = ops
+        self.last_counts = None
+
+    def __call__(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                 weight_before_down: bool = False) -> torch.Tensor:
+        G, d = self.world, x.shape[1]
+        p = self.ops.dispatch(x, ids, weights, weight_before_down)
+        send_counts = p.expert_counts.view(G, self.e_local).sum(dim=1).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        both = torch.stack([send_counts, recv_counts]).cpu()
+        sc, rc = both[0].tolist(), both[1].tolist()
+        self.last_counts = (sc, rc)
+        n_send, n_recv = sum(sc), sum(rc)
+        recv_x = torch.empty((n_recv, d), dtype=x.dtype, device=x.device)
+        dist.all_to_all_single(recv_x, p.send_x[:n_send].contiguous(), rc, sc, group=self.group)
+        meta = torch.stack([p.send_expert[:n_send], p.send_weight[:n_send].view(torch.int32)], dim=1).contiguous()
+        recv_meta = torch.empty((n_recv, 2), dtype=torch.int32, device=x.device)
+        dist.all_to_all_single(recv_meta, meta, rc, sc, group=self.group)
+        local_ids = (recv_meta[:, 0] - self.base).to(torch.int32).reshape(-1, 1).contiguous()
+        if weight_before_down:
+            rw = recv_meta[:, 1].contiguous().view(torch.float32).reshape(-1, 1).contiguous()
+        else:
+            rw = torch.ones((n_recv, 1), dtype=torch.float32, device=x.device)
+        y = self.ops.local_ffn(recv_x, local_ids, rw, weight_before_down)
+        y_back = torch.empty((max(n_send, 1), d), dtype=torch.float32, device=x.device)
+        dist.all_to_all_single(y_back[:n_send], y.contiguous(), sc, rc, group=self.group)
+        return self.ops.combine(p, y_back)

@@ -277,7 +277,10 @@ class ExpertSet:
                     raise ValueError(f"expert factor {k} has shape [{fr.rows},{fr.cols}], expected rows/cols "
                                      f"consistent with {want}")
         self.n_expert, self.n_embd, self.n_ff, self.rank = len(experts), d, f, rank
-        self.device = torch.device(device)
+        dev = torch.device(device)
+        if dev.type == "cuda" and dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
         self.factors = {k: StackedFactor([ex[k].padded(*shapes[k]) for ex in experts], self.device) for k in KINDS}
 
     def __getitem__(self, kind: str) -> StackedFactor:

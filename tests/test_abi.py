@@ -53,6 +53,8 @@ def test_workspace_size_and_validation(lib):
     n = C.c_size_t()
     assert lib.latent_expert_ffn_workspace_size(C.byref(dsc), C.byref(n)) == 0
     assert n.value > 0 and n.value % 256 == 0
+    empty = _desc(T=0)         # empty batch: valid, small workspace
+    assert lib.latent_expert_ffn_workspace_size(C.byref(empty), C.byref(n)) == 0
     bad = _desc(d=48)          # not a multiple of 32
     assert lib.latent_expert_ffn_workspace_size(C.byref(bad), C.byref(n)) == 2
     bad = _desc(r=96)          # unsupported padded rank
