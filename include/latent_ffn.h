@@ -186,6 +186,19 @@ LATENT_API int latent_expert_ffn_workspace_size(const latent_ffn_desc *desc, siz
  * latent_expert_ffn_check(). */
 LATENT_API int latent_expert_ffn_forward(const latent_ffn_desc *desc, struct CUstream_st *stream);
 
+/* latent_expert_ffn_forward for callers that cannot allocate device memory
+ * at call time (a host framework that plans all buffers before running its
+ * graph and forbids allocation during it, real-time hosts that reserve all
+ * memory up front, processes under a hard GPU memory cap).  No counterpart
+ * in the reference op.  It ignores desc->workspace and uses a 16 MiB scratch
+ * array that the library keeps in device memory (reserved on every GPU that
+ * loads the library, until exit); a call needing more returns
+ * LATENT_ERR_WORKSPACE.  The first call on a device resolves the array's
+ * address and should come before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race.  Device-side errors of this
+ * variant are not reported.  Allocates nothing. */
+LATENT_API int latent_expert_ffn_forward_noalloc(const latent_ffn_desc *desc, struct CUstream_st *stream);
+
 /* latent_expert_ffn_forward that also records the caller's events on
  * `stream` around each kernel it launches: events[0] before routing, then one
  * after routing and after every FFN kernel (decode: 4 phases + combine, so 7
