@@ -19,10 +19,12 @@
  *                                              even column in the low nibble
  *                                              (loader/latent_loader.py:129)
  *   scales  fp16   [n_expert][rows][cols/32]  one scale per 32-element group
- *                                              along a row
+ *                                              along a row; scales are >= 0,
+ *                                              and the sign bit flags an
+ *                                              INT8 group
  *   NF4 group:  value = NF4_LEVEL[code] * float(scale)
- *   INT8 group: value = float(int8(hi << 4 | lo)) * float(scale), where lo is
- *               the 4-bit code in `codes` and hi comes from `i8_hi`.
+ *   INT8 group: value = float(int8(hi << 4 | lo)) * float(|scale|), where lo
+ *               is the 4-bit code in `codes` and hi comes from `i8_hi`.
  *   i8_mask uint32 [n_expert][mask_words]     bit g%32 of word g/32 set when
  *                                              expert-local group g (= row *
  *                                              cols/32 + col/32) is INT8;

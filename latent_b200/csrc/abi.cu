@@ -82,9 +82,12 @@ int validate(const latent_ffn_desc *d, bool need_ptrs) {
     return LATENT_OK;
 }
 
+// AUTO: the tensor-core path once an expert sees ~64 rows on average (a
+// 128-row MMA tile is then at least half full); the CUDA-core chain below.
 int pick_path(const latent_ffn_desc *d) {
     if (d->path != LATENT_PATH_AUTO) return d->path;
-    return LATENT_PATH_DECODE;
+    const int64_t R = (int64_t)d->n_tokens * d->top_k;
+    return (R >= 4096 && R >= 64 * (int64_t)d->n_expert) ? LATENT_PATH_PREFILL : LATENT_PATH_DECODE;
 }
 
 DecodeArgs decode_args(const latent_ffn_desc *d) {
@@ -111,7 +114,7 @@ DecodeArgs decode_args(const latent_ffn_desc *d) {
     return a;
 }
 
-Layout layout(const latent_ffn_desc *d, const DecodeArgs &a) {
+Layout layout(const latent_ffn_desc *d, const DecodeArgs &a, int path) {
     Layout L{};
     const size_t E = (size_t)d->n_expert, R = (size_t)d->n_tokens * (size_t)d->top_k;
     size_t o = 0;
@@ -120,13 +123,13 @@ Layout layout(const latent_ffn_desc *d, const DecodeArgs &a) {
     L.offsets = o;       o = align_up(o + (E + 1) * 4);
     L.active = o;        o = align_up(o + E * 4);
     L.n_active = o;      o = align_up(o + 4);
-    L.n_sem = (int)(2 * E);
+    L.n_sem = path == LATENT_PATH_PREFILL ? 0 : decode_sem_count(a);
     L.sem = o;           o = align_up(o + (size_t)L.n_sem * 4);
     L.order = o;         o = align_up(o + R * 4);
     L.pos = o;           o = align_up(o + R * 4);
     L.block_counts = o;  o = align_up(o + route_block_counts_bytes((int)E, (int)R));
     L.scratch = o;
-    o = align_up(o + decode_scratch_floats(a) * sizeof(float));
+    o = align_up(o + (path == LATENT_PATH_PREFILL ? prefill_scratch_bytes(a) : decode_scratch_floats(a) * sizeof(float)));
     L.total = o;
     return L;
 }
@@ -167,7 +170,7 @@ extern "C" LATENT_API int latent_expert_ffn_workspace_size(const latent_ffn_desc
     const int st = validate(desc, false);
     if (st) return st;
     const DecodeArgs a = decode_args(desc);
-    *bytes = layout(desc, a).total;
+    *bytes = layout(desc, a, pick_path(desc)).total;
     return LATENT_OK;
 }
 
@@ -178,9 +181,8 @@ int forward_impl(const latent_ffn_desc *desc, CUstream_st *stream, Marks *marks)
     if (st) return st;
     if (desc->n_tokens == 0) return LATENT_OK;
     const int path = pick_path(desc);
-    if (path == LATENT_PATH_PREFILL) return LATENT_ERR_UNSUPPORTED;
     DecodeArgs a = decode_args(desc);
-    const Layout L = layout(desc, a);
+    const Layout L = layout(desc, a, path);
     if (!desc->workspace || desc->workspace_bytes < L.total) return LATENT_ERR_WORKSPACE;
     if (!aligned(desc->workspace, kAlign)) return LATENT_ERR_ALIGN;
     void *ws = desc->workspace;
@@ -213,6 +215,7 @@ int forward_impl(const latent_ffn_desc *desc, CUstream_st *stream, Marks *marks)
     a.rt.pos = ra.pos;
     a.rt.sem = ra.sem;
     a.rt.err = ra.err;
+    if (path == LATENT_PATH_PREFILL) return cuda_status(launch_prefill(a, at<void>(ws, L.scratch), s, marks));
     float *f = at<float>(ws, L.scratch);
     const size_t R = (size_t)a.R, r = (size_t)a.r;
     a.part1 = f;  f += (size_t)a.ks1 * R * 2 * r;
@@ -221,6 +224,14 @@ int forward_impl(const latent_ffn_desc *desc, CUstream_st *stream, Marks *marks)
     a.part2 = f;  f += (size_t)a.ks2 * R * r;
     a.s = f;      f += R * r;
     a.y = f;
+    uint32_t *sem = ra.sem;
+    a.work = sem;       sem += 1;
+    a.arr1 = sem;       sem += a.E;
+    a.flag1 = sem;      sem += a.E;
+    a.cnt2 = sem;       sem += a.E;
+    a.arr3 = sem;       sem += a.E;
+    a.flag3 = sem;      sem += a.E;
+    a.tokcnt = sem;
     return cuda_status(launch_decode(a, s, marks));
 }
 
@@ -276,7 +287,7 @@ Layout ep_layout(const latent_ep_desc *d) {
     f.n_tokens = d->n_tokens;
     f.top_k = d->top_k;
     DecodeArgs a = decode_args(&f);
-    Layout L = layout(&f, a);
+    Layout L = layout(&f, a, LATENT_PATH_PREFILL);
     L.total = L.scratch;
     return L;
 }

@@ -1,22 +1,34 @@
 // Decode path: the latent expert FFN as a chain of quantized vector-matrix
-// products on CUDA cores with fp32 accumulation (rel-L2 <= 1e-5 vs the
-// fp32 reference runtime, loader/latent_runtime.py:35-59).
+// products on CUDA cores with fp32 accumulation (rel-L2 <= 1e-5 vs the fp32
+// reference runtime, loader/latent_runtime.py:35-59).
 //
-// Per active expert e with n_e routed tokens (contiguous routed positions):
-//   phase 1  t = x . [A_g | A_u]        K = d split in ks1 row chunks (split-K)
-//   phase 2  h = silu(t_g . B_g) * (t_u . B_u) [* w]   column tiles of f
-//   phase 3  s = h . A_d                K = f split in ks2 row chunks
-//   phase 4  y = s . B_d                column tiles of d
-//   combine  out[t] = sum_j w_tj * y_(t,j)  in slot order
-// Split-K partials are summed in chunk order by the last CTA that finishes
-// an expert (arrival counter, no waiting), so results are deterministic.
+// One persistent, cooperatively launched kernel runs the whole chain.  Work
+// items are handed out in phase order by an atomic counter:
+//   phase 1  t = x . [A_g | A_u]   item = (expert, matrix, row chunk of d)  split-K
+//   phase 2  h = silu(t_g.B_g) * (t_u.B_u) [* w]   item = (expert, 256-column tile of f)
+//   phase 3  s = h . A_d           item = (expert, row chunk of f)          split-K
+//   phase 4  y = s . B_d           item = (expert, 256-column tile of d), fused top-k combine
+// An item waits (bounded) only for its own expert's previous phase:
+// phase-1/3 partial sums are reduced in chunk order by the last item to
+// arrive (arrival counter), which then publishes a ready flag; phase 3 waits
+// for all phase-2 tiles of its expert; the last phase-4 tile to finish a
+// (token, column tile) sums that token's top-k rows in slot order.  Items are
+// handed out in phase order and every CTA is resident (cooperative launch),
+// so every wait ends; a wait that exceeds its bound sets kErrTimeout and the
+// kernel runs to completion without waiting further.  Results are bitwise
+// deterministic.
 //
-// Every factor element is read from HBM exactly once per call (per token
-// chunk of up to 4 tokens).  A lane owns 16 consecutive columns of a row
-// (8 code bytes, half of one 32-element scale group): it decodes each 4-bit
-// code through a 16-entry shared-memory table (the 16 entries sit in 16
-// distinct banks, so a warp's lookup is one wavefront) and accumulates
-// x*scale*level with packed fp32x2 FMAs.
+// Inner loop: codes and scales stream through a 4-deep cp.async ring in
+// shared memory (memory parallelism independent of registers).  A lane owns
+// 16 consecutive columns of a row (8 code bytes, half a 32-element scale
+// group), turns codes into table byte offsets with one shift and one
+// and-or per 8 codes, looks each value up in a shared table and accumulates
+// x*scale*value with packed fp32x2 FMAs on 64-bit accumulators.  The table
+// has the 16 NF4 levels in banks 0-15 and the identity 0..15 in banks 16-31;
+// the sign bit of a group's scale (set for INT8 groups) selects the second,
+// so a warp lookup is one wavefront and INT8 groups cost the hot loop nothing
+// extra.  The INT8 high nibbles are added afterwards to the CTA's reduced
+// tile (int8_fix), in a fixed order.
 #include "internal.h"
 
 namespace latent {
@@ -26,126 +38,219 @@ namespace {
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTileN = 256;  // output columns per tile on the output side
+constexpr unsigned long long kWaitNs = 2000000000ull;  // a dependency wait gives up after 2 s
 
-__device__ __forceinline__ void fma2(float &a0, float &a1, float x, float v0, float v1) {
-    unsigned long long acc, xx, vv;
-    asm("mov.b64 %0, {%1,%2};" : "=l"(acc) : "f"(a0), "f"(a1));
-    asm("mov.b64 %0, {%1,%1};" : "=l"(xx) : "f"(x));
-    asm("mov.b64 %0, {%1,%2};" : "=l"(vv) : "f"(v0), "f"(v1));
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(xx), "l"(vv));
-    asm("mov.b64 {%0,%1}, %2;" : "=f"(a0), "=f"(a1) : "l"(acc));
+typedef unsigned long long u64;
+
+__device__ __forceinline__ u64 pack2(float a, float b) {
+    u64 r;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
 }
 
-__device__ __forceinline__ uint2 ldg_stream_v2(const void *p) {
-    uint2 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-    return v;
+__device__ __forceinline__ void unpack2(u64 v, float &a, float &b) {
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
 }
 
-// One row of a lane's 16 columns: acc[t][j] += in[t] * scale * value(j).
-template <int NT>
-__device__ __forceinline__ void row_fma(const QView &M, int64_t group, int half, uint2 q, uint16_t sbits,
-                                        const float *xin, int xstride, const float *lut, float (&acc)[NT][16]) {
-    const float sc = half_bits_to_float(sbits);
-    float xs[NT];
-#pragma unroll
-    for (int t = 0; t < NT; ++t) xs[t] = xin[t * xstride] * sc;
-    uint32_t idx;
-    if (M.i8.present() && M.i8.is_int8(group, &idx)) {
-        const uint2 hi = *reinterpret_cast<const uint2 *>(M.i8.hi + (int64_t)idx * 16 + half * 8);
-#pragma unroll
-        for (int w = 0; w < 2; ++w) {
-            const uint32_t lo_w = w ? q.y : q.x, hi_w = w ? hi.y : hi.x;
-#pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                const float v0 = int8_elem(lo_w, hi_w, i), v1 = int8_elem(lo_w, hi_w, i + 1);
-#pragma unroll
-                for (int t = 0; t < NT; ++t) fma2(acc[t][8 * w + i], acc[t][8 * w + i + 1], xs[t], v0, v1);
-            }
+__device__ __forceinline__ void ffma2(u64 &acc, u64 x, u64 v) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(x), "l"(v));
+}
+
+__device__ __forceinline__ float lut_at(const float *lut, uint32_t byte_off) {
+    return *reinterpret_cast<const float *>(reinterpret_cast<const char *>(lut) + byte_off);
+}
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int b) { return __byte_perm(w, 0u, 0x4440u | b); }
+
+// Bounded wait until *flag >= target (thread 0 of the CTA only).  Returns
+// false (and records kErrTimeout) when the bound is exceeded or another CTA
+// already gave up.
+__device__ bool wait_ge(const uint32_t *flag, uint32_t target, uint32_t *err) {
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    unsigned ns = 32;
+    while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (v >= target) return true;
+        uint32_t e;
+        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(e) : "l"(err) : "memory");
+        if (e & kErrTimeout) return false;
+        unsigned long long now;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+        if (now - t0 > kWaitNs) {
+            atomicOr(err, kErrTimeout);
+            return false;
         }
-        return;
+        __nanosleep(ns);
+        if (ns < 1024) ns <<= 1;
+    }
+}
+
+// cp.async (LDGSTS) helpers.
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void cp_async16(void *s, const void *g) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(s)), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *s, const void *g) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(s)), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int kStages = 4;
+constexpr int kWarpStageCode = 1024;  // code bytes per warp per stage
+constexpr int kWarpStageScale = 256;  // scale bytes per warp per stage
+constexpr int kWarpStageBytes = kWarpStageCode + kWarpStageScale;
+constexpr int kWarpRing = kStages * kWarpStageBytes;
+constexpr int kStageBytes = kWarps * kWarpRing / kStages;  // per-CTA bytes of one stage (all warps)
+
+// One staged row of a lane's 16 columns: acc[t][p] (columns 2p, 2p+1) += in[t]*scale*table[code].
+// `tsel` adds 64 bytes to every table offset: the identity table that decodes
+// the low nibble of an INT8 group (its high nibble is added by int8_fix).
+template <int NT>
+__device__ __forceinline__ void row_fma(uint2 q, uint32_t tsel, float sc, const float *xin, int xstride,
+                                        const float *lut, u64 (&acc)[NT][8]) {
+    u64 xs[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const float v = xin[t * xstride] * sc;
+        xs[t] = pack2(v, v);
     }
 #pragma unroll
-    for (int w = 0; w < 2; ++w) {
-        const uint32_t word = w ? q.y : q.x;
+    for (int w2 = 0; w2 < 2; ++w2) {
+        const uint32_t word = w2 ? q.y : q.x;
+        const uint32_t e4 = ((word << 2) & 0x3C3C3C3Cu) | tsel;  // even columns: table byte offsets
+        const uint32_t o4 = ((word >> 2) & 0x3C3C3C3Cu) | tsel;  // odd columns
 #pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-            const float v0 = lut[(word >> (4 * i)) & 15u];
-            const float v1 = lut[(word >> (4 * i + 4)) & 15u];
+        for (int j = 0; j < 4; ++j) {
+            const u64 vv = pack2(lut_at(lut, byte_of(e4, j)), lut_at(lut, byte_of(o4, j)));
 #pragma unroll
-            for (int t = 0; t < NT; ++t) fma2(acc[t][8 * w + i], acc[t][8 * w + i + 1], xs[t], v0, v1);
+            for (int t = 0; t < NT; ++t) ffma2(acc[t][4 * w2 + j], xs[t], vv);
         }
     }
 }
 
 // Accumulates rows [row0, row_end) x columns [col0, col0+ncols) of M against
 // in_s[t * in_ld + (row - row0)] into the calling lane's 16-column slice.
-// Lanes: LPR lanes span a row (16 columns each), 32/LPR rows per warp step.
+// Each warp streams its own contiguous share of the rows through a private
+// kStages-deep cp.async ring in `stages` (kWarpRing bytes per warp), so the
+// loop synchronises only within the warp.  LPR lanes span a row (16 columns
+// each), 32/LPR rows per warp step.  All threads of the CTA must call it.
 template <int LPR, int NT>
-__device__ __forceinline__ void vecmat_accum(const QView &M, int row0, int row_end, int col0, int ncols,
-                                             const float *in_s, int in_ld, const float *lut,
-                                             float (&acc)[NT][16]) {
+__device__ __forceinline__ void vecmat_staged(const QView &M, int row0, int row_end, int col0, int ncols,
+                                              const float *in_s, int in_ld, const float *lut, uint8_t *stages,
+                                              u64 (&acc)[NT][8]) {
     constexpr int RPW = 32 / LPR;
-    constexpr int STEP = kWarps * RPW;
-    constexpr int U = 4;
 #pragma unroll
     for (int t = 0; t < NT; ++t)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[t][j] = 0.f;
+        for (int j = 0; j < 8; ++j) acc[t][j] = 0ull;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int cl = (lane % LPR) * 16;
-    if (cl >= ncols) return;
-    const int c = col0 + cl;
+    const int cb = ncols >> 1, ng = ncols >> 5;
+    const int spitch = (ng * 2 + 3) & ~3;
+    // this warp's rows: a multiple of RPW
+    const int nrows = row_end - row0;
+    const int per = (nrows + kWarps * RPW - 1) / (kWarps * RPW) * RPW;
+    const int wr0 = row0 + warp * per, wr1 = min(row_end, wr0 + per);
+    uint8_t *ring = stages + warp * kWarpRing;
+    int SR = kWarpStageCode / cb;
+    if (SR * spitch > kWarpStageScale) SR = kWarpStageScale / spitch;
+    SR = SR / RPW * RPW;
+    const int nst = wr1 > wr0 ? (wr1 - wr0 + SR - 1) / SR : 0;
     const int64_t rb = M.cols >> 1, gpr = M.cols >> 5;
-    const uint8_t *cp = M.codes + (c >> 1);
-    const uint16_t *sp = M.scales + (c >> 5);
-    const int half = (c >> 4) & 1;
-    int row = row0 + warp * RPW + lane / LPR;
-    for (; row + (U - 1) * STEP < row_end; row += U * STEP) {
-        uint2 q[U];
-        uint16_t sb[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            q[u] = ldg_stream_v2(cp + (int64_t)(row + u * STEP) * rb);
-            sb[u] = __ldg(sp + (int64_t)(row + u * STEP) * gpr);
+    const bool sc4 = ((gpr | ng | (col0 >> 5)) & 1) == 0;
+    const int chunks = cb >> 4;
+    const int cshift = (chunks & (chunks - 1)) == 0 ? __ffs(chunks) - 1 : -1;
+    const int n4 = ng >> 1;
+    const int sshift = (n4 & (n4 - 1)) == 0 && n4 > 0 ? __ffs(n4) - 1 : -1;
+    const uint8_t *gcodes = M.codes + (col0 >> 1);
+    const uint16_t *gscales = M.scales + (col0 >> 5);
+
+    auto issue = [&](int s) {
+        if (s < nst) {
+            uint8_t *buf = ring + (s % kStages) * kWarpStageBytes;
+            const int rbase = wr0 + s * SR;
+            const int nr = min(SR, wr1 - rbase);
+            for (int i = lane; i < nr * chunks; i += 32) {
+                const int rr = cshift >= 0 ? i >> cshift : i / chunks;
+                const int ch = i - rr * chunks;
+                cp_async16(buf + rr * cb + ch * 16, gcodes + (int64_t)(rbase + rr) * rb + ch * 16);
+            }
+            uint8_t *sbuf = buf + kWarpStageCode;
+            if (sc4) {
+                for (int i = lane; i < nr * n4; i += 32) {
+                    const int rr = sshift >= 0 ? i >> sshift : i / n4;
+                    const int ch = i - rr * n4;
+                    cp_async4(sbuf + rr * spitch + ch * 4, gscales + (int64_t)(rbase + rr) * gpr + ch * 2);
+                }
+            } else {
+                for (int i = lane; i < nr * ng; i += 32) {
+                    const int rr = i / ng, gi = i - rr * ng;
+                    *reinterpret_cast<uint16_t *>(sbuf + rr * spitch + gi * 2) =
+                        __ldg(gscales + (int64_t)(rbase + rr) * gpr + gi);
+                }
+            }
         }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int rr = row + u * STEP;
-            row_fma<NT>(M, (int64_t)rr * gpr + (c >> 5), half, q[u], sb[u], in_s + (rr - row0), in_ld, lut, acc);
+        cp_commit();
+    };
+
+    for (int s = 0; s < kStages - 1; ++s) issue(s);
+    const int cl = (lane % LPR) * 16;
+    const int rs = lane / LPR;
+    for (int s = 0; s < nst; ++s) {
+        cp_wait<kStages - 2>();
+        __syncwarp();
+        issue(s + kStages - 1);
+        if (cl < ncols) {
+            const uint8_t *buf = ring + (s % kStages) * kWarpStageBytes;
+            const uint8_t *sbuf = buf + kWarpStageCode;
+            const int rbase = wr0 + s * SR;
+            const int nr = min(SR, wr1 - rbase);
+            const float *xin = in_s + (rbase - row0);
+            for (int rr = rs; rr < nr; rr += RPW) {
+                const uint2 q = *reinterpret_cast<const uint2 *>(buf + rr * cb + (cl >> 1));
+                const uint16_t sb = *reinterpret_cast<const uint16_t *>(sbuf + rr * spitch + (cl >> 5) * 2);
+                const uint32_t tsel = (sb & 0x8000u) ? 0x40404040u : 0u;
+                row_fma<NT>(q, tsel, half_bits_to_float(sb & 0x7FFFu), xin + rr, in_ld, lut, acc);
+            }
         }
+        __syncwarp();
     }
-    for (; row < row_end; row += STEP) {
-        const uint2 q = ldg_stream_v2(cp + (int64_t)row * rb);
-        const uint16_t sb = __ldg(sp + (int64_t)row * gpr);
-        row_fma<NT>(M, (int64_t)row * gpr + (c >> 5), half, q, sb, in_s + (row - row0), in_ld, lut, acc);
-    }
+    cp_wait<0>();
+    __syncthreads();
 }
 
-// Sums the lanes that share columns (across the 32/LPR row lanes of a warp,
-// then across warps through red_s[kWarps][NT][LPR*16]).  After the call,
-// red_s[0..NT*ncols) -- indexed t * (LPR*16) + col -- holds the CTA's sums.
+// Sums lanes that share columns (the 32/LPR row lanes of a warp, then the
+// warps through red_s[kWarps][NT][W], W = LPR*16).  The CTA's sums end up at
+// red_s + kWarps*NT*W, indexed t*W + col.
 template <int LPR, int NT>
-__device__ __forceinline__ void cta_reduce(float (&acc)[NT][16], int ncols, float *red_s) {
+__device__ __forceinline__ float *cta_reduce(u64 (&acc)[NT][8], int ncols, float *red_s) {
     constexpr int W = LPR * 16;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float a[NT][16];
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int p = 0; p < 8; ++p) unpack2(acc[t][p], a[t][2 * p], a[t][2 * p + 1]);
 #pragma unroll
     for (int o = LPR; o < 32; o <<= 1)
 #pragma unroll
         for (int t = 0; t < NT; ++t)
 #pragma unroll
-            for (int j = 0; j < 16; ++j) acc[t][j] += __shfl_xor_sync(0xffffffffu, acc[t][j], o);
+            for (int j = 0; j < 16; ++j) a[t][j] += __shfl_xor_sync(0xffffffffu, a[t][j], o);
     const int cl = lane * 16;
     if (lane < LPR && cl < ncols) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
             float4 *dst = reinterpret_cast<float4 *>(red_s + (warp * NT + t) * W + cl);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                dst[j] = make_float4(acc[t][4 * j], acc[t][4 * j + 1], acc[t][4 * j + 2], acc[t][4 * j + 3]);
+            for (int j = 0; j < 4; ++j) dst[j] = make_float4(a[t][4 * j], a[t][4 * j + 1], a[t][4 * j + 2], a[t][4 * j + 3]);
         }
     }
     __syncthreads();
+    float *res = red_s + kWarps * NT * W;
     for (int i = threadIdx.x; i < NT * W; i += kThreads) {
         const int col = i % W;
         float v = 0.f;
@@ -153,177 +258,267 @@ __device__ __forceinline__ void cta_reduce(float (&acc)[NT][16], int ncols, floa
 #pragma unroll
             for (int w = 0; w < kWarps; ++w) v += red_s[w * NT * W + i];
         }
-        red_s[kWarps * NT * W + i] = v;
+        res[i] = v;
     }
+    __syncthreads();
+    return res;
+}
+
+// Does expert e's factor have any INT8 group?  (prefix counts of the stacked tensor)
+__device__ __forceinline__ bool expert_has_int8(const latent_qmatrix &m, int e) {
+    if (!m.i8_mask) return false;
+    const int64_t words = ((m.rows * m.cols >> 5) + 31) >> 5;
+    const uint32_t *mask = m.i8_mask + (int64_t)e * words;
+    const uint32_t *base = m.i8_base + (int64_t)e * words;
+    const uint32_t first = __ldg(base), last = __ldg(base + words - 1) + __popc(__ldg(mask + words - 1));
+    return last > first;
+}
+
+// Adds the high-nibble part of every INT8 group of the tile to the CTA's
+// reduced sums res[t * W + col] (the main loop decoded only the low nibble,
+// through the identity table): value = (16*h + l) * |scale| with h the
+// signed high nibble from the i8_hi side table.  Deterministic: thread
+// (column chunk of 8, row slice) accumulates its rows in order, then the
+// slices are summed in order.  `part` needs 8*NT*W floats, `scratch` 20.5 KB.
+template <int NT>
+__device__ void int8_fix(const QView &M, int row0, int row_end, int col0, int ncols, const float *in_s, int in_ld,
+                         float *res, int W, float *part, uint8_t *scratch) {
+    const int ng = ncols >> 5, g0 = col0 >> 5;
+    const int64_t gpr = M.cols >> 5;
+    const int64_t words = (((int64_t)M.rows * gpr) + 31) >> 5;
+    const int ccount = ncols >> 3;
+    const int slices = min(8, kThreads / ccount);
+    const int cc = threadIdx.x % ccount, sl = threadIdx.x / ccount;
+    const bool active = sl < slices;
+    const int col8 = cc * 8, gi = col8 >> 5, wsel = (col8 & 31) >> 3;
+    uint32_t *bits_s = reinterpret_cast<uint32_t *>(scratch);           // [64]
+    uint4 *hi_s = reinterpret_cast<uint4 *>(scratch + 256);             // [64][16]
+    float *sc_s = reinterpret_cast<float *>(scratch + 256 + 64 * 16 * 16);  // [64][16]
+    float acc[NT][8];
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[t][j] = 0.f;
+    for (int rc = row0; rc < row_end; rc += 64) {
+        const int nr = min(64, row_end - rc);
+        __syncthreads();
+        if ((int)threadIdx.x < nr) {
+            const int row = rc + threadIdx.x;
+            const int64_t pos = (int64_t)row * gpr + g0;
+            const int64_t w = pos >> 5;
+            const int b = (int)(pos & 31);
+            uint64_t two = __ldg(M.i8.mask + w);
+            if (b + ng > 32 && w + 1 < words) two |= (uint64_t)__ldg(M.i8.mask + w + 1) << 32;
+            const uint32_t bits = (uint32_t)(two >> b) & ((1u << ng) - 1u);
+            bits_s[threadIdx.x] = bits;
+            for (uint32_t rest = bits; rest; rest &= rest - 1) {
+                const int q = __ffs(rest) - 1;
+                const int64_t p2 = pos + q;
+                const uint32_t mw = __ldg(M.i8.mask + (p2 >> 5));
+                const uint32_t idx = __ldg(M.i8.base + (p2 >> 5)) + __popc(mw & ((1u << (p2 & 31)) - 1u));
+                cp_async16(hi_s + threadIdx.x * 16 + q, M.i8.hi + (int64_t)idx * 16);
+                sc_s[threadIdx.x * 16 + q] = 16.f * half_bits_to_float(__ldg(M.scales + p2) & 0x7FFFu);
+            }
+        }
+        cp_commit();
+        cp_wait<0>();
+        __syncthreads();
+        if (active) {
+            for (int rr = sl; rr < nr; rr += slices) {
+                if (!((bits_s[rr] >> gi) & 1u)) continue;
+                const uint32_t hw = reinterpret_cast<const uint32_t *>(hi_s + rr * 16 + gi)[wsel];
+                const float s16 = sc_s[rr * 16 + gi];
+                float xv[NT];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) xv[t] = in_s[t * in_ld + (rc - row0 + rr)] * s16;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float h = (float)((int)(((hw >> (4 * j)) & 15u) ^ 8u) - 8);
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) acc[t][j] = fmaf(xv[t], h, acc[t][j]);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (active) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) part[(sl * NT + t) * W + col8 + j] = acc[t][j];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+        for (int col = threadIdx.x; col < ncols; col += kThreads) {
+            float s = 0.f;
+            for (int q = 0; q < slices; ++q) s += part[(q * NT + t) * W + col];
+            res[t * W + col] += s;
+        }
     __syncthreads();
 }
 
-__device__ __forceinline__ void init_lut(float *lut) {
-    if (threadIdx.x < 16) lut[threadIdx.x] = kNF4Levels[threadIdx.x];
+struct Smem {
+    float *lut;    // 32: NF4 levels, then the identity table 0..15
+    uint8_t *stages;  // kStages * kStageBytes
+    float *in_s;   // staged input vectors
+    float *red_s;  // (kWarps+1) * 4 * max(r, kTileN)
+    float *g_s;    // 4 * kTileN
+    int *list;     // kThreads token ids
+    int *flag;     // 2 ints
+};
+
+__device__ __forceinline__ void cta_wait(const uint32_t *flag, uint32_t target, const DecodeArgs &a, const Smem &S) {
+    if (threadIdx.x == 0) wait_ge(flag, target, a.rt.err);
+    __syncthreads();
 }
 
-}  // namespace
+// Publishes this CTA's global writes, then adds 1 to *ctr; returns the old value (all threads).
+__device__ __forceinline__ uint32_t cta_arrive(uint32_t *ctr, const Smem &S) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) S.flag[0] = (int)atomicAdd(ctr, 1u);
+    __syncthreads();
+    return (uint32_t)S.flag[0];
+}
 
-namespace {
-
-// Runs one token chunk of the input side (split-K) and stores the chunk's
-// partial sums; NT is picked at run time from the chunk size.
 template <int LPR, int NT>
-__device__ __forceinline__ void in_chunk(const QView &M, int row0, int row_end, int r, const float *in_s, int kc,
-                                         const float *lut, float *red_s, float *part_rows, int ldo) {
-    float acc[NT][16];
-    vecmat_accum<LPR, NT>(M, row0, row_end, 0, r, in_s, kc, lut, acc);
-    cta_reduce<LPR, NT>(acc, r, red_s);
-    const float *res = red_s + kWarps * NT * r;
-    for (int i = threadIdx.x; i < NT * r; i += kThreads) {
-        const int t = i / r, col = i - t * r;
-        part_rows[(int64_t)t * ldo + col] = res[i];
-    }
+__device__ __forceinline__ void in_chunk(const QView &M, bool has_i8, int row0, int row_end, int r, const float *in_s,
+                                         int kc, const Smem &S, float *part_rows, int ldo) {
+    u64 acc[NT][8];
+    vecmat_staged<LPR, NT>(M, row0, row_end, 0, r, in_s, kc, S.lut, S.stages, acc);
+    float *res = cta_reduce<LPR, NT>(acc, r, S.red_s);
+    if (has_i8) int8_fix<NT>(M, row0, row_end, 0, r, in_s, kc, res, LPR * 16, S.red_s, S.stages);
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+        for (int col = threadIdx.x; col < r; col += kThreads) part_rows[(int64_t)t * ldo + col] = res[t * r + col];
 }
 
-// Phases 1 and 3: t = x.[A_g|A_u] (PH=1) or s = h.A_d (PH=3), split-K.
+// Phase 1 (PH=1: t = x.A_{g|u}) and phase 3 (PH=3: s = h.A_d): one split-K row chunk.
 template <int LPR, int XT, int PH>
-__global__ void __launch_bounds__(kThreads) k_in_phase(DecodeArgs a) {
-    extern __shared__ float sm[];
-    __shared__ int s_last;
+__device__ void item_in(const DecodeArgs &a, const Smem &S, int ai, int m, int ksel) {
     constexpr int nmat = PH == 1 ? 2 : 1;
-    const int kc = PH == 1 ? a.kc1 : a.kc2;
-    const int ks = PH == 1 ? a.ks1 : a.ks2;
-    const int r = a.r;
-    float *lut = sm;
-    float *in_s = sm + 32;
-    float *red_s = in_s + 4 * kc;
-    int w = blockIdx.x;
-    const int ksel = w % ks;
-    w /= ks;
-    const int m = w % nmat;
-    const int ai = w / nmat;
-    init_lut(lut);
-    if (ai >= *a.rt.n_active) return;
+    const int kc = PH == 1 ? a.kc1 : a.kc2, ks = PH == 1 ? a.ks1 : a.ks2, r = a.r;
     const int e = a.rt.active[ai];
     const int p0 = a.rt.offsets[e], ne = a.rt.offsets[e + 1] - p0;
+    if (PH == 3) cta_wait(a.cnt2 + e, (uint32_t)a.nct_f, a, S);
     const latent_qmatrix &qm = PH == 1 ? (m == 0 ? a.gate_a : a.up_a) : a.down_a;
     const QView M = expert_view(qm, e);
+    const bool has_i8 = expert_has_int8(qm, e);
     const int row0 = ksel * kc, row_end = min(M.rows, row0 + kc);
     const int ldo = nmat * r;
     float *part = PH == 1 ? a.part1 : a.part2;
     for (int tc = 0; tc < ne; tc += 4) {
         const int nt = min(4, ne - tc);
         __syncthreads();
-        for (int i = threadIdx.x; i < nt * kc; i += kThreads) {
-            const int t = i / kc, rr = i - t * kc, row = row0 + rr;
-            float v = 0.f;
-            if (row < row_end) {
-                const int p = p0 + tc + t;
-                if constexpr (PH == 1) {
-                    const int tok = a.rt.order[p] / a.k;
-                    v = load_act<XT>(a.x, (int64_t)tok * a.d + row);
-                } else {
-                    v = a.h[(int64_t)p * a.f + row];
+        for (int t = 0; t < nt; ++t) {
+            const int p = p0 + tc + t;
+            const int64_t src = PH == 1 ? (int64_t)(a.rt.order[p] / a.k) * a.d : (int64_t)p * a.f;
+            for (int rr = threadIdx.x; rr < kc; rr += kThreads) {
+                const int row = row0 + rr;
+                float v = 0.f;
+                if (row < row_end) {
+                    if constexpr (PH == 1)
+                        v = load_act<XT>(a.x, src + row);
+                    else
+                        v = __ldcg(a.h + src + row);
                 }
+                S.in_s[t * kc + rr] = v;
             }
-            in_s[i] = v;
         }
         __syncthreads();
         float *rows = part + ((int64_t)ksel * a.R + p0 + tc) * ldo + m * r;
         if (nt == 1)
-            in_chunk<LPR, 1>(M, row0, row_end, r, in_s, kc, lut, red_s, rows, ldo);
+            in_chunk<LPR, 1>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo);
         else if (nt == 2)
-            in_chunk<LPR, 2>(M, row0, row_end, r, in_s, kc, lut, red_s, rows, ldo);
+            in_chunk<LPR, 2>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo);
         else if (nt == 3)
-            in_chunk<LPR, 3>(M, row0, row_end, r, in_s, kc, lut, red_s, rows, ldo);
+            in_chunk<LPR, 3>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo);
         else
-            in_chunk<LPR, 4>(M, row0, row_end, r, in_s, kc, lut, red_s, rows, ldo);
+            in_chunk<LPR, 4>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo);
     }
-    // Arrival: the last CTA of this expert sums the split-K partials in order.
-    __threadfence();
-    __syncthreads();
-    uint32_t *sem = a.rt.sem + (PH == 1 ? 0 : a.E) + e;
-    if (threadIdx.x == 0) s_last = atomicAdd(sem, 1u) == (uint32_t)(nmat * ks - 1);
-    __syncthreads();
-    if (!s_last) return;
+    uint32_t *arr = (PH == 1 ? a.arr1 : a.arr3) + e;
+    if (cta_arrive(arr, S) != (uint32_t)(nmat * ks - 1)) return;
+    // Last chunk of this expert: sum the partials in chunk order, publish.
     __threadfence();
     float *outv = PH == 1 ? a.t : a.s;
-    for (int i = threadIdx.x; i < ne * ldo; i += kThreads) {
-        const int pp = p0 + i / ldo, col = i % ldo;
-        float v = 0.f;
-        for (int q = 0; q < ks; ++q) v += __ldcg(part + ((int64_t)q * a.R + pp) * ldo + col);
-        outv[(int64_t)pp * ldo + col] = v;
+    for (int pp = p0; pp < p0 + ne; ++pp) {
+        for (int col = threadIdx.x; col < ldo; col += kThreads) {
+            float v = 0.f;
+            for (int q = 0; q < ks; ++q) v += __ldcg(part + ((int64_t)q * a.R + pp) * ldo + col);
+            outv[(int64_t)pp * ldo + col] = v;
+        }
     }
-    if (threadIdx.x == 0) *sem = 0u;
+    cta_arrive(PH == 1 ? a.flag1 + e : a.flag3 + e, S);
 }
 
 template <int NT>
-__device__ __forceinline__ void gateup_chunk(const DecodeArgs &a, const QView &Mg, const QView &Mu, int col0,
-                                             int ncols, int p, const float *in_g, const float *in_u,
-                                             const float *lut, float *red_s, float *g_s) {
+__device__ __forceinline__ void gateup_chunk(const DecodeArgs &a, const Smem &S, const QView &Mg, bool gi8,
+                                             const QView &Mu, bool ui8, int col0, int ncols, int p,
+                                             const float *in_g, const float *in_u) {
     constexpr int W = kTileN;
     const int r = a.r;
-    float acc[NT][16];
-    vecmat_accum<16, NT>(Mg, 0, r, col0, ncols, in_g, r, lut, acc);
-    cta_reduce<16, NT>(acc, ncols, red_s);
-    const float *res = red_s + kWarps * NT * W;
-    for (int i = threadIdx.x; i < NT * W; i += kThreads) g_s[i] = res[i];
+    u64 acc[NT][8];
+    vecmat_staged<16, NT>(Mg, 0, r, col0, ncols, in_g, r, S.lut, S.stages, acc);
+    float *res = cta_reduce<16, NT>(acc, ncols, S.red_s);
+    if (gi8) int8_fix<NT>(Mg, 0, r, col0, ncols, in_g, r, res, W, S.red_s, S.stages);
+    for (int i = threadIdx.x; i < NT * W; i += kThreads) S.g_s[i] = res[i];
     __syncthreads();
-    vecmat_accum<16, NT>(Mu, 0, r, col0, ncols, in_u, r, lut, acc);
-    cta_reduce<16, NT>(acc, ncols, red_s);
+    vecmat_staged<16, NT>(Mu, 0, r, col0, ncols, in_u, r, S.lut, S.stages, acc);
+    res = cta_reduce<16, NT>(acc, ncols, S.red_s);
+    if (ui8) int8_fix<NT>(Mu, 0, r, col0, ncols, in_u, r, res, W, S.red_s, S.stages);
     const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
     for (int i = threadIdx.x; i < NT * W; i += kThreads) {
         const int t = i / W, col = i - t * W;
         if (col >= ncols) continue;
-        float hv = silu_f32(g_s[i]) * res[i];
+        float hv = silu_f32(S.g_s[i]) * res[i];
         if (wbd) hv *= load_weight(a.weights, a.w_type, a.rt.order[p + t]);
         a.h[(int64_t)(p + t) * a.f + col0 + col] = hv;
     }
 }
 
-// Phase 2: h = silu(t_g.B_g) * (t_u.B_u) [* w], one 256-column tile of f.
-__global__ void __launch_bounds__(kThreads) k_gateup_out(DecodeArgs a) {
-    extern __shared__ float sm[];
+// Phase 2: h = silu(t_g.B_g) * (t_u.B_u) [* w] for one 256-column tile of f.
+__device__ void item_gateup(const DecodeArgs &a, const Smem &S, int ai, int ct) {
     const int r = a.r;
-    float *lut = sm;
-    float *in_g = sm + 32;
-    float *in_u = in_g + 4 * r;
-    float *red_s = in_u + 4 * r;
-    float *g_s = red_s + (kWarps + 1) * 4 * kTileN;
-    const int nct = (a.f + kTileN - 1) / kTileN;
-    const int ct = blockIdx.x % nct, ai = blockIdx.x / nct;
-    init_lut(lut);
-    if (ai >= *a.rt.n_active) return;
     const int e = a.rt.active[ai];
     const int p0 = a.rt.offsets[e], ne = a.rt.offsets[e + 1] - p0;
+    cta_wait(a.flag1 + e, 1u, a, S);
     const QView Mg = expert_view(a.gate_b, e), Mu = expert_view(a.up_b, e);
+    const bool gi8 = expert_has_int8(a.gate_b, e), ui8 = expert_has_int8(a.up_b, e);
     const int col0 = ct * kTileN, ncols = min(kTileN, a.f - col0);
+    float *in_g = S.in_s, *in_u = S.in_s + 4 * r;
     for (int tc = 0; tc < ne; tc += 4) {
         const int nt = min(4, ne - tc);
         __syncthreads();
-        for (int i = threadIdx.x; i < nt * r; i += kThreads) {
-            const int t = i / r, kk = i - t * r;
+        for (int t = 0; t < nt; ++t) {
             const float *src = a.t + (int64_t)(p0 + tc + t) * 2 * r;
-            in_g[i] = src[kk];
-            in_u[i] = src[r + kk];
+            for (int kk = threadIdx.x; kk < r; kk += kThreads) {
+                in_g[t * r + kk] = __ldcg(src + kk);
+                in_u[t * r + kk] = __ldcg(src + r + kk);
+            }
         }
         __syncthreads();
         const int p = p0 + tc;
         if (nt == 1)
-            gateup_chunk<1>(a, Mg, Mu, col0, ncols, p, in_g, in_u, lut, red_s, g_s);
+            gateup_chunk<1>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u);
         else if (nt == 2)
-            gateup_chunk<2>(a, Mg, Mu, col0, ncols, p, in_g, in_u, lut, red_s, g_s);
+            gateup_chunk<2>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u);
         else if (nt == 3)
-            gateup_chunk<3>(a, Mg, Mu, col0, ncols, p, in_g, in_u, lut, red_s, g_s);
+            gateup_chunk<3>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u);
         else
-            gateup_chunk<4>(a, Mg, Mu, col0, ncols, p, in_g, in_u, lut, red_s, g_s);
+            gateup_chunk<4>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u);
     }
+    cta_arrive(a.cnt2 + e, S);
 }
 
 template <int NT>
-__device__ __forceinline__ void down_chunk(const DecodeArgs &a, const QView &M, int col0, int ncols, int p,
-                                           const float *in_s, const float *lut, float *red_s) {
+__device__ __forceinline__ void down_chunk(const DecodeArgs &a, const Smem &S, const QView &M, bool i8, int col0,
+                                           int ncols, int p) {
     constexpr int W = kTileN;
-    float acc[NT][16];
-    vecmat_accum<16, NT>(M, 0, a.r, col0, ncols, in_s, a.r, lut, acc);
-    cta_reduce<16, NT>(acc, ncols, red_s);
-    const float *res = red_s + kWarps * NT * W;
+    u64 acc[NT][8];
+    vecmat_staged<16, NT>(M, 0, a.r, col0, ncols, S.in_s, a.r, S.lut, S.stages, acc);
+    float *res = cta_reduce<16, NT>(acc, ncols, S.red_s);
+    if (i8) int8_fix<NT>(M, 0, a.r, col0, ncols, S.in_s, a.r, res, W, S.red_s, S.stages);
     const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
     for (int i = threadIdx.x; i < NT * W; i += kThreads) {
         const int t = i / W, col = i - t * W;
@@ -335,42 +530,214 @@ __device__ __forceinline__ void down_chunk(const DecodeArgs &a, const QView &M, 
     }
 }
 
-// Phase 4: y = s.B_d, one 256-column tile of d.
-__global__ void __launch_bounds__(kThreads) k_down_out(DecodeArgs a) {
-    extern __shared__ float sm[];
+__device__ __forceinline__ int live_slots(const DecodeArgs &a, int t) {
+    int n = 0;
+    for (int j = 0; j < a.k; ++j) n += a.rt.pos[t * a.k + j] >= 0;
+    return n;
+}
+
+// Phase 4: y = s.B_d for one 256-column tile of d, then the top-k combine of
+// every token whose last routed slot for this tile just finished.
+__device__ void item_down(const DecodeArgs &a, const Smem &S, int ai, int ct) {
     const int r = a.r;
-    float *lut = sm;
-    float *in_s = sm + 32;
-    float *red_s = in_s + 4 * r;
-    const int nct = (a.d + kTileN - 1) / kTileN;
-    const int ct = blockIdx.x % nct, ai = blockIdx.x / nct;
-    init_lut(lut);
-    if (ai >= *a.rt.n_active) return;
     const int e = a.rt.active[ai];
     const int p0 = a.rt.offsets[e], ne = a.rt.offsets[e + 1] - p0;
+    cta_wait(a.flag3 + e, 1u, a, S);
     const QView M = expert_view(a.down_b, e);
+    const bool i8 = expert_has_int8(a.down_b, e);
     const int col0 = ct * kTileN, ncols = min(kTileN, a.d - col0);
     for (int tc = 0; tc < ne; tc += 4) {
         const int nt = min(4, ne - tc);
         __syncthreads();
-        for (int i = threadIdx.x; i < nt * r; i += kThreads) {
-            const int t = i / r, kk = i - t * r;
-            in_s[i] = a.s[(int64_t)(p0 + tc + t) * r + kk];
-        }
+        for (int t = 0; t < nt; ++t)
+            for (int kk = threadIdx.x; kk < r; kk += kThreads)
+                S.in_s[t * r + kk] = __ldcg(a.s + (int64_t)(p0 + tc + t) * r + kk);
         __syncthreads();
         const int p = p0 + tc;
         if (nt == 1)
-            down_chunk<1>(a, M, col0, ncols, p, in_s, lut, red_s);
+            down_chunk<1>(a, S, M, i8, col0, ncols, p);
         else if (nt == 2)
-            down_chunk<2>(a, M, col0, ncols, p, in_s, lut, red_s);
+            down_chunk<2>(a, S, M, i8, col0, ncols, p);
         else if (nt == 3)
-            down_chunk<3>(a, M, col0, ncols, p, in_s, lut, red_s);
+            down_chunk<3>(a, S, M, i8, col0, ncols, p);
         else
-            down_chunk<4>(a, M, col0, ncols, p, in_s, lut, red_s);
+            down_chunk<4>(a, S, M, i8, col0, ncols, p);
+    }
+    if (a.flags & LATENT_FLAG_OUT_PER_SLOT) return;
+    __threadfence();
+    const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
+    for (int base = 0; base < ne; base += kThreads) {
+        __syncthreads();
+        if (threadIdx.x == 0) S.flag[1] = 0;
+        __syncthreads();
+        const int i = base + threadIdx.x;
+        if (i < ne) {
+            const int t = a.rt.order[p0 + i] / a.k;
+            const uint32_t old = atomicAdd(a.tokcnt + (int64_t)t * a.nct_d + ct, 1u);
+            if ((int)old + 1 == live_slots(a, t)) S.list[atomicAdd(&S.flag[1], 1)] = t;
+        }
+        __syncthreads();
+        const int n_done = S.flag[1];
+        if (n_done == 0) continue;
+        __threadfence();
+        for (int q = 0; q < n_done; ++q) {
+            const int t = S.list[q];
+            for (int col = threadIdx.x; col < ncols; col += kThreads) {
+                float acc = 0.f;
+                for (int j = 0; j < a.k; ++j) {
+                    const int slot = t * a.k + j;
+                    const int pp = a.rt.pos[slot];
+                    if (pp < 0) continue;
+                    const float w = wbd ? 1.f : load_weight(a.weights, a.w_type, slot);
+                    acc = fmaf(w, __ldcg(a.y + (int64_t)pp * a.d + col0 + col), acc);
+                }
+                a.out[(int64_t)t * a.d + col0 + col] = acc;
+            }
+        }
     }
 }
 
-// Top-k combine in slot order (or zero rows of skipped slots in per-slot mode).
+template <int LPR, int XT>
+__global__ void __launch_bounds__(kThreads, 2) k_decode(DecodeArgs a) {
+    extern __shared__ __align__(128) uint8_t sm_raw[];
+    __shared__ __align__(128) float s_lut[32];
+    __shared__ int s_list[kThreads];
+    __shared__ int s_flag[2];
+    __shared__ int s_item;
+    Smem S;
+    S.lut = s_lut;
+    S.stages = sm_raw;
+    float *sm = reinterpret_cast<float *>(sm_raw + kStages * kStageBytes);
+    S.in_s = sm;
+    S.red_s = sm + a.in_floats;
+    S.g_s = S.red_s + a.red_floats;
+    S.list = s_list;
+    S.flag = s_flag;
+    if (threadIdx.x < 16) s_lut[threadIdx.x] = kNF4Levels[threadIdx.x];
+    else if (threadIdx.x < 32) s_lut[threadIdx.x] = (float)(threadIdx.x - 16);
+    const int n_active = *a.rt.n_active;
+    const int n1 = n_active * 2 * a.ks1, n2 = n_active * a.nct_f, n3 = n_active * a.ks2, n4 = n_active * a.nct_d;
+    // Rows no expert writes: skipped slots (per-slot output) or tokens with no live slot.
+    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
+    const int n_rows = per_slot ? a.T * a.k : a.T;
+    for (int i = blockIdx.x; i < n_rows; i += gridDim.x) {
+        const bool empty = per_slot ? a.rt.pos[i] < 0 : live_slots(a, i) == 0;
+        if (empty)
+            for (int c = threadIdx.x * 4; c < a.d; c += kThreads * 4)
+                *reinterpret_cast<float4 *>(a.out + (int64_t)i * a.d + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    while (true) {
+        __syncthreads();
+        if (threadIdx.x == 0) s_item = (int)atomicAdd(a.work, 1u);
+        __syncthreads();
+        int it = s_item;
+        if (it < n1) {
+            item_in<LPR, XT, 1>(a, S, it / (2 * a.ks1), (it / a.ks1) % 2, it % a.ks1);
+            continue;
+        }
+        it -= n1;
+        if (it < n2) {
+            item_gateup(a, S, it / a.nct_f, it % a.nct_f);
+            continue;
+        }
+        it -= n2;
+        if (it < n3) {
+            item_in<LPR, LATENT_TYPE_F32, 3>(a, S, it / a.ks2, 0, it % a.ks2);
+            continue;
+        }
+        it -= n3;
+        if (it < n4) {
+            item_down(a, S, it / a.nct_d, it % a.nct_d);
+            continue;
+        }
+        break;
+    }
+}
+
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// Rows per split-K item: about 32 KB of codes, whole warp steps, at most 1024.
+void plan_split(int K, int r, int &kc, int &ks) {
+    const int lpr = r / 16;
+    const int step = kWarps * (32 / lpr);
+    int rows = 32768 / (r / 2);
+    rows = rows < step ? step : rows;
+    rows = rows > 1024 ? 1024 : rows;
+    kc = round_up(rows, 64);
+    if (kc > round_up(K, 64)) kc = round_up(K, 64);
+    ks = (K + kc - 1) / kc;
+}
+
+template <int LPR>
+const void *decode_fn(int x_type) {
+    switch (x_type) {
+        case LATENT_TYPE_F32: return (const void *)k_decode<LPR, LATENT_TYPE_F32>;
+        case LATENT_TYPE_F16: return (const void *)k_decode<LPR, LATENT_TYPE_F16>;
+        default: return (const void *)k_decode<LPR, LATENT_TYPE_BF16>;
+    }
+}
+
+const void *pick_decode_fn(int r, int x_type) {
+    switch (r) {
+        case 32: return decode_fn<2>(x_type);
+        case 64: return decode_fn<4>(x_type);
+        case 128: return decode_fn<8>(x_type);
+        case 256: return decode_fn<16>(x_type);
+        case 512: return decode_fn<32>(x_type);
+        default: return nullptr;
+    }
+}
+
+}  // namespace
+
+void decode_plan(DecodeArgs &a) {
+    a.R = a.T * a.k;
+    a.nmax = a.E < a.R ? a.E : a.R;
+    a.nct_f = (a.f + kTileN - 1) / kTileN;
+    a.nct_d = (a.d + kTileN - 1) / kTileN;
+    plan_split(a.d, a.r, a.kc1, a.ks1);
+    plan_split(a.f, a.r, a.kc2, a.ks2);
+    int in_f = 4 * (a.kc1 > a.kc2 ? a.kc1 : a.kc2);
+    if (in_f < 8 * a.r) in_f = 8 * a.r;
+    a.in_floats = round_up(in_f, 32);
+    const int w = a.r > kTileN ? a.r : kTileN;
+    a.red_floats = (kWarps + 1) * 4 * w;
+}
+
+int decode_sem_count(const DecodeArgs &a) { return 1 + 5 * a.E + a.T * a.nct_d; }
+
+size_t decode_scratch_floats(const DecodeArgs &a) {
+    const size_t R = (size_t)a.R, r = (size_t)a.r;
+    return (size_t)a.ks1 * R * 2 * r + R * 2 * r + R * (size_t)a.f + (size_t)a.ks2 * R * r + R * r +
+           R * (size_t)a.d + 6 * 64;
+}
+
+cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t s, Marks *marks) {
+    const void *fn = pick_decode_fn(a.r, a.x_type);
+    if (!fn) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)kStages * kStageBytes + (size_t)(a.in_floats + a.red_floats + 4 * kTileN) * sizeof(float);
+    cudaError_t err = ensure_smem(fn, smem);
+    if (err != cudaSuccess) return err;
+    int dev = 0, sms = 0, per_sm = 0;
+    if ((err = cudaGetDevice(&dev)) != cudaSuccess) return err;
+    if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return err;
+    if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem)) != cudaSuccess) return err;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const int grid = sms * per_sm;
+    void *args[] = {(void *)&a};
+    err = cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kThreads), args, smem, s);
+    if (marks) marks->mark(s);
+    return err;
+}
+
+}  // namespace latent
+
+namespace latent {
+
+namespace {
+
+// Top-k combine of per-routed-row outputs in slot order (used by the
+// expert-parallel return path), or zero rows of skipped slots in per-slot mode.
 __global__ void __launch_bounds__(256) k_combine(DecodeArgs a) {
     const int t = blockIdx.y;
     const int c = (blockIdx.x * 256 + threadIdx.x) * 4;
@@ -396,106 +763,7 @@ __global__ void __launch_bounds__(256) k_combine(DecodeArgs a) {
     if (!per_slot) *reinterpret_cast<float4 *>(a.out + (int64_t)t * a.d + c) = acc;
 }
 
-int round_up(int x, int m) { return (x + m - 1) / m * m; }
-
-void plan_split(int K, int nmax, int nmat, int step, int &kc, int &ks) {
-    const int target = 2 * 148;
-    int want = (target + nmax * nmat - 1) / (nmax * nmat);
-    want = want < 1 ? 1 : want;
-    const int unit = step > 64 ? step : 64;
-    kc = round_up((K + want - 1) / want, unit);
-    if (kc > 1024) kc = 1024;
-    if (kc < unit) kc = unit;
-    ks = (K + kc - 1) / kc;
-}
-
-template <int LPR>
-cudaError_t launch_in_phases(const DecodeArgs &a, int ph, cudaStream_t s) {
-    const size_t smem = (32 + 4 * (ph == 1 ? a.kc1 : a.kc2) + (kWarps + 1) * 4 * a.r) * sizeof(float);
-    const int grid = a.nmax * (ph == 1 ? 2 * a.ks1 : a.ks2);
-    const void *fn;
-    if (ph == 1) {
-        switch (a.x_type) {
-            case LATENT_TYPE_F32: fn = (const void *)k_in_phase<LPR, LATENT_TYPE_F32, 1>; break;
-            case LATENT_TYPE_F16: fn = (const void *)k_in_phase<LPR, LATENT_TYPE_F16, 1>; break;
-            default: fn = (const void *)k_in_phase<LPR, LATENT_TYPE_BF16, 1>; break;
-        }
-    } else {
-        fn = (const void *)k_in_phase<LPR, LATENT_TYPE_F32, 3>;
-    }
-    cudaError_t err = ensure_smem(fn, smem);
-    if (err != cudaSuccess) return err;
-    void *args[] = {(void *)&a};
-    return cudaLaunchKernel(fn, dim3(grid), dim3(kThreads), args, smem, s);
-}
-
-cudaError_t launch_in(const DecodeArgs &a, int ph, cudaStream_t s) {
-    switch (a.r) {
-        case 32: return launch_in_phases<2>(a, ph, s);
-        case 64: return launch_in_phases<4>(a, ph, s);
-        case 128: return launch_in_phases<8>(a, ph, s);
-        case 256: return launch_in_phases<16>(a, ph, s);
-        case 512: return launch_in_phases<32>(a, ph, s);
-        default: return cudaErrorInvalidValue;
-    }
-}
-
 }  // namespace
-
-void decode_plan(DecodeArgs &a) {
-    a.R = a.T * a.k;
-    a.nmax = a.E < a.R ? a.E : a.R;
-    if (a.nmax < 1) {  // empty batch: nothing is launched
-        a.kc1 = a.kc2 = 64;
-        a.ks1 = a.ks2 = 1;
-        return;
-    }
-    const int lpr = a.r / 16;
-    const int step = kWarps * (32 / (lpr > 32 ? 32 : lpr));
-    plan_split(a.d, a.nmax, 2, step, a.kc1, a.ks1);
-    plan_split(a.f, a.nmax, 1, step, a.kc2, a.ks2);
-}
-
-size_t decode_scratch_floats(const DecodeArgs &a) {
-    const size_t R = (size_t)a.R, r = (size_t)a.r;
-    return (size_t)a.ks1 * R * 2 * r + R * 2 * r + R * (size_t)a.f + (size_t)a.ks2 * R * r + R * r +
-           R * (size_t)a.d + 6 * 64;
-}
-
-cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t s, Marks *marks) {
-    Marks none;
-    Marks &m = marks ? *marks : none;
-    cudaError_t err;
-    if ((err = launch_in(a, 1, s)) != cudaSuccess) return err;
-    m.mark(s);
-    {
-        const size_t smem = (32 + 8 * a.r + (kWarps + 1) * 4 * kTileN + 4 * kTileN) * sizeof(float);
-        if ((err = ensure_smem((const void *)k_gateup_out, smem)) != cudaSuccess) return err;
-        const int grid = a.nmax * ((a.f + kTileN - 1) / kTileN);
-        k_gateup_out<<<grid, kThreads, smem, s>>>(a);
-        if ((err = cudaGetLastError()) != cudaSuccess) return err;
-    }
-    m.mark(s);
-    if ((err = launch_in(a, 3, s)) != cudaSuccess) return err;
-    m.mark(s);
-    {
-        const size_t smem = (32 + 4 * a.r + (kWarps + 1) * 4 * kTileN) * sizeof(float);
-        if ((err = ensure_smem((const void *)k_down_out, smem)) != cudaSuccess) return err;
-        const int grid = a.nmax * ((a.d + kTileN - 1) / kTileN);
-        k_down_out<<<grid, kThreads, smem, s>>>(a);
-        if ((err = cudaGetLastError()) != cudaSuccess) return err;
-    }
-    m.mark(s);
-    dim3 grid((a.d / 4 + 255) / 256, a.T);
-    k_combine<<<grid, 256, 0, s>>>(a);
-    err = cudaGetLastError();
-    m.mark(s);
-    return err;
-}
-
-}  // namespace latent
-
-namespace latent {
 
 cudaError_t launch_combine(const DecodeArgs &a, cudaStream_t s) {
     if (a.T == 0) return cudaSuccess;

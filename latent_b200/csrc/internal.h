@@ -66,7 +66,19 @@ struct DecodeArgs {
     int nmax;      // upper bound on active experts: min(E, R)
     int kc1, ks1;  // rows per split-K chunk / chunks, x -> t
     int kc2, ks2;  // rows per split-K chunk / chunks, h -> s
+    int nct_f, nct_d;          // 256-column tiles of f and d
+    int in_floats, red_floats;  // shared-memory carve-up of the fused kernel
+    // Counters in the routing block's zeroed region (decode_sem_count of them):
+    uint32_t *work;    // [1] next work item
+    uint32_t *arr1;    // [E] phase-1 chunk arrivals
+    uint32_t *flag1;   // [E] t of the expert is complete
+    uint32_t *cnt2;    // [E] finished phase-2 tiles
+    uint32_t *arr3;    // [E] phase-3 chunk arrivals
+    uint32_t *flag3;   // [E] s of the expert is complete
+    uint32_t *tokcnt;  // [T][nct_d] finished slots per (token, d tile)
 };
+
+int decode_sem_count(const DecodeArgs &a);
 
 // Optional caller events recorded between kernel launches (profiling).
 struct Marks {
@@ -82,6 +94,10 @@ struct Marks {
 void decode_plan(DecodeArgs &a);
 size_t decode_scratch_floats(const DecodeArgs &a);
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t s, Marks *marks);
+
+// Prefill path (tcgen05 grouped GEMMs); scratch is prefill_scratch_bytes(a) bytes.
+size_t prefill_scratch_bytes(const DecodeArgs &a);
+cudaError_t launch_prefill(const DecodeArgs &a, void *scratch, cudaStream_t s, Marks *marks);
 
 // Top-k combine of per-routed-row outputs (a.y) into a.out, slot order.
 cudaError_t launch_combine(const DecodeArgs &a, cudaStream_t s);

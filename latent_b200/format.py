@@ -185,8 +185,11 @@ class StackedFactor:
         dev = torch.device(device)
         E, g = len(factors), rows * cols // GROUP
         self.codes = torch.stack([f.lo.to(dev) for f in factors]).reshape(E, rows, cols // 2).contiguous()
-        self.scales = torch.stack([f.scales.to(dev) for f in factors]).reshape(E, rows, cols // GROUP).contiguous()
         is_i8 = torch.stack([f.is_int8.to(dev) for f in factors]).reshape(E, g)
+        # INT8 groups carry the sign bit of their (non-negative) fp16 scale as a flag.
+        sc = torch.stack([f.scales.to(dev) for f in factors]).reshape(E, g)
+        sc = torch.where(is_i8, sc | torch.tensor(-0x8000, dtype=torch.int16, device=dev), sc)
+        self.scales = sc.reshape(E, rows, cols // GROUP).contiguous()
         self.int8_per_expert = is_i8.sum(dim=1).cpu().tolist()
         self.n_int8 = int(sum(self.int8_per_expert))
         if self.n_int8:
@@ -229,7 +232,7 @@ class StackedFactor:
         """Copy of expert ``e`` as a GroupedFactor (host side; for tests and tooling)."""
         g = self.rows * self.cols // GROUP
         lo = self.codes[e].reshape(self.rows, self.cols // GROUP, 16).cpu()
-        sc = self.scales[e].cpu()
+        sc = self.scales[e].cpu() & 0x7FFF
         i8 = torch.zeros(g, dtype=torch.bool)
         hi = torch.zeros((g, 16), dtype=torch.uint8)
         if self.n_int8:
