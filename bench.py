@@ -60,6 +60,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bound on the CPU baseline's timed work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill leg of the default run")
     return ap.parse_args()
 
 
@@ -327,7 +328,61 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_leg(cfg, es, x, ids, w, args.cpu_seconds)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if world == 1 and args.config == 1 and not args.no_prefill:
+        del es, op
+        torch.cuda.empty_cache()
+        line["prefill"] = run_prefill(args, 2, dev, steps=max(5, min(args.steps, 20)), warmup=args.warmup)
     return line
+
+
+PREFILL_PHASES = ["route", "dequant+gather", "G1 x.[A_g|A_u]", "G2 silu(t_g.B_g)*(t_u.B_u)", "G3 h.A_d",
+                  "G4 s.B_d", "combine"]
+
+
+def run_prefill(args, cfg_id: int, dev, steps: int, warmup: int):
+    """Prefill leg (tcgen05 path): per-kernel CUDA-event times, tensor-core roofline."""
+    from latent_b200 import ExpertFFN
+    cfg, es, x, ids, w, gen_s = workload(cfg_id, dev, 0)
+    op = ExpertFFN(es, path="prefill")
+    flush = L2Flush(dev)
+    for _ in range(max(warmup, 3)):
+        op(x, ids, w)
+    op.check()
+    n_marks = len(PREFILL_PHASES) + 1
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_marks)] for _ in range(steps)]
+    for row in evs:
+        for e in row:
+            e.record()
+    torch.cuda.synchronize()
+    for k in range(steps):
+        flush()
+        op.call_timed(x, ids, w, evs[k])
+    torch.cuda.synchronize()
+    seg = np.array([[evs[k][i].elapsed_time(evs[k][i + 1]) for i in range(n_marks - 1)] for k in range(steps)])
+    phase_ms = seg.mean(axis=0)
+    total = float(seg.sum(axis=1).mean())
+    R = int((ids >= 0).sum())
+    d, f, r = cfg.n_embd, cfg.n_ff, cfg.rank
+    flops = {2: 2 * d * 2 * r * R, 3: 2 * r * 2 * f * R, 4: 2 * f * r * R, 5: 2 * r * d * R}
+    dom = max(flops, key=lambda i: phase_ms[i])
+    pk = peaks()
+    ach = flops[dom] / (phase_ms[dom] * 1e-3) / 1e12
+    all_flops = sum(flops.values())
+    gemm_ms = float(sum(phase_ms[i] for i in flops))
+    return {
+        "workload": cfg.name, "value": R / (total * 1e-3), "unit": UNIT, "ms_per_step": total, "steps": steps,
+        "routed": R, "dtype": "f16 MMA, f32 accumulate",
+        "roofline": {"bound": "tensor", "kernel": PREFILL_PHASES[dom], "achieved": ach, "peak": pk["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"], "traffic": None, "flops": flops[dom],
+                     "mean_ms": float(phase_ms[dom]), "peak_source": pk["source"] + " (burst bf16 GEMM)"},
+        "roofline_gemms": {"achieved": all_flops / (gemm_ms * 1e-3) / 1e12, "flops": all_flops,
+                           "frac": all_flops / (gemm_ms * 1e-3) / 1e12 / pk["bf16_tflops"], "unit": "TFLOP/s"},
+        "roofline_step": {"achieved": all_flops / (total * 1e-3) / 1e12,
+                          "frac": all_flops / (total * 1e-3) / 1e12 / pk["bf16_tflops"], "unit": "TFLOP/s"},
+        "phase_ms": {PREFILL_PHASES[i]: float(phase_ms[i]) for i in range(len(PREFILL_PHASES))},
+        "gpu_launches": steps * ((1 if ids.numel() <= 4096 else 3) + 8 + 4 + 1),
+        "gen_s": gen_s,
+    }
 
 
 class _TimedOps:

@@ -67,6 +67,12 @@ __device__ __forceinline__ float silu_f32(float x) {
     return x / (1.0f + expf(-x));
 }
 
+// SiLU with the fast exponential and division (about 2 ulp); used where the
+// result is rounded to f16 anyway (the prefill epilogue).
+__device__ __forceinline__ float silu_fast(float x) {
+    return __fdividef(x, 1.0f + __expf(-x));
+}
+
 // Per-group INT8 lookup for a stacked factor: is group g (expert-local) INT8,
 // and where are its high nibbles?
 struct Int8Side {

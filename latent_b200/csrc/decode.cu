@@ -138,7 +138,12 @@ __device__ __forceinline__ void row_fma(uint2 q, uint32_t tsel, float sc, const 
 // kStages-deep cp.async ring in `stages` (kWarpRing bytes per warp), so the
 // loop synchronises only within the warp.  LPR lanes span a row (16 columns
 // each), 32/LPR rows per warp step.  All threads of the CTA must call it.
-template <int LPR, int NT>
+// phase: kFull (prologue + loop), kPrologue (issue the first kStages-1
+// stages and return: lets an item start streaming weights before it waits for
+// its inputs), kLoop (the rest; the same geometry's prologue was issued).
+enum : int { kFull = 0, kPrologue = 1, kLoop = 2 };
+
+template <int LPR, int NT, int PHASE = kFull>
 __device__ __forceinline__ void vecmat_staged(const QView &M, int row0, int row_end, int col0, int ncols,
                                               const float *in_s, int in_ld, const float *lut, uint8_t *stages,
                                               u64 (&acc)[NT][8]) {
@@ -196,7 +201,9 @@ __device__ __forceinline__ void vecmat_staged(const QView &M, int row0, int row_
         cp_commit();
     };
 
-    for (int s = 0; s < kStages - 1; ++s) issue(s);
+    if (PHASE != kLoop)
+        for (int s = 0; s < kStages - 1; ++s) issue(s);
+    if (PHASE == kPrologue) return;
     const int cl = (lane % LPR) * 16;
     const int rs = lane / LPR;
     for (int s = 0; s < nst; ++s) {
@@ -277,9 +284,17 @@ __device__ __forceinline__ bool expert_has_int8(const latent_qmatrix &m, int e) 
 // Adds the high-nibble part of every INT8 group of the tile to the CTA's
 // reduced sums res[t * W + col] (the main loop decoded only the low nibble,
 // through the identity table): value = (16*h + l) * |scale| with h the
-// signed high nibble from the i8_hi side table.  Deterministic: thread
-// (column chunk of 8, row slice) accumulates its rows in order, then the
-// slices are summed in order.  `part` needs 8*NT*W floats, `scratch` 20.5 KB.
+// signed high nibble from the i8_hi side table.  Per chunk of 256 rows it
+// makes two round trips to memory: (1) the mask and prefix words of every
+// row, (2) the high-nibble records and scale words of every INT8 group.
+// Deterministic: thread (column chunk of 8, row slice) accumulates its rows
+// in order, then the slices are summed in order.  `part` needs 8*NT*W
+// floats; `scratch` kI8Scratch bytes.
+constexpr int kI8Rows = 256;
+constexpr int kI8Cap = 512;
+constexpr int kI8Scratch = kI8Rows * 16 + kI8Rows * 8 + 64 + kI8Cap * 20;
+static_assert(kI8Rows == kThreads, "int8_fix scans one row per thread");
+
 template <int NT>
 __device__ void int8_fix(const QView &M, int row0, int row_end, int col0, int ncols, const float *in_s, int in_ld,
                          float *res, int W, float *part, uint8_t *scratch) {
@@ -291,33 +306,76 @@ __device__ void int8_fix(const QView &M, int row0, int row_end, int col0, int nc
     const int cc = threadIdx.x % ccount, sl = threadIdx.x / ccount;
     const bool active = sl < slices;
     const int col8 = cc * 8, gi = col8 >> 5, wsel = (col8 & 31) >> 3;
-    uint32_t *bits_s = reinterpret_cast<uint32_t *>(scratch);           // [64]
-    uint4 *hi_s = reinterpret_cast<uint4 *>(scratch + 256);             // [64][16]
-    float *sc_s = reinterpret_cast<float *>(scratch + 256 + 64 * 16 * 16);  // [64][16]
+    uint32_t *msk = reinterpret_cast<uint32_t *>(scratch);                    // [kI8Rows][2]
+    uint32_t *bas = msk + 2 * kI8Rows;                                         // [kI8Rows][2]
+    uint32_t *rowbits = bas + 2 * kI8Rows;                                     // [kI8Rows]
+    int *rowstart = reinterpret_cast<int *>(rowbits + kI8Rows);                // [kI8Rows + 1 + kWarps]
+    uint4 *ent_hi = reinterpret_cast<uint4 *>(scratch + kI8Rows * 16 + kI8Rows * 8 + 64);  // [kI8Cap]
+    float *ent_sc = reinterpret_cast<float *>(ent_hi + kI8Cap);               // [kI8Cap] 16*|scale|
     float acc[NT][8];
 #pragma unroll
     for (int t = 0; t < NT; ++t)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[t][j] = 0.f;
-    for (int rc = row0; rc < row_end; rc += 64) {
-        const int nr = min(64, row_end - rc);
+    for (int rc = row0; rc < row_end;) {
+        int nr = min(kI8Rows, row_end - rc);
         __syncthreads();
-        if ((int)threadIdx.x < nr) {
-            const int row = rc + threadIdx.x;
-            const int64_t pos = (int64_t)row * gpr + g0;
+        // round trip 1: mask and prefix words of each row's tile groups
+        for (int i = threadIdx.x; i < nr; i += kThreads) {
+            const int64_t pos = (int64_t)(rc + i) * gpr + g0;
             const int64_t w = pos >> 5;
+            cp_async4(msk + 2 * i, M.i8.mask + w);
+            cp_async4(bas + 2 * i, M.i8.base + w);
+            if ((int)(pos & 31) + ng > 32 && w + 1 < words) {
+                cp_async4(msk + 2 * i + 1, M.i8.mask + w + 1);
+                cp_async4(bas + 2 * i + 1, M.i8.base + w + 1);
+            } else {
+                msk[2 * i + 1] = 0u;
+            }
+        }
+        cp_commit();
+        cp_wait<0>();
+        __syncthreads();
+        {   // one row per thread (kI8Rows == kThreads): bits, then a block scan of their counts
+            const int i = threadIdx.x, lane = i & 31, wid = i >> 5;
+            uint32_t bits = 0u;
+            if (i < nr) {
+                const int64_t pos = (int64_t)(rc + i) * gpr + g0;
+                const int b = (int)(pos & 31);
+                const uint64_t two = (uint64_t)msk[2 * i] | ((uint64_t)msk[2 * i + 1] << 32);
+                bits = (uint32_t)(two >> b) & ((1u << ng) - 1u);
+                rowbits[i] = bits;
+            }
+            const int c = __popc(bits);
+            int v = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += y;
+            }
+            if (lane == 31) rowstart[kI8Rows + 1 + wid] = v;  // warp totals (scratch slots)
+            __syncthreads();
+            int base = 0;
+            for (int w2 = 0; w2 < wid; ++w2) base += rowstart[kI8Rows + 1 + w2];
+            const int start = base + v - c;
+            const bool ok = i < nr && start + c <= kI8Cap;
+            __syncthreads();
+            if (ok) rowstart[i] = start;
+            nr = __syncthreads_count(ok);  // rows handled this pass (a prefix of the chunk)
+        }
+        // round trip 2: high-nibble records and scale words of the INT8 groups
+        for (int i = threadIdx.x; i < nr; i += kThreads) {
+            const int64_t pos = (int64_t)(rc + i) * gpr + g0;
             const int b = (int)(pos & 31);
-            uint64_t two = __ldg(M.i8.mask + w);
-            if (b + ng > 32 && w + 1 < words) two |= (uint64_t)__ldg(M.i8.mask + w + 1) << 32;
-            const uint32_t bits = (uint32_t)(two >> b) & ((1u << ng) - 1u);
-            bits_s[threadIdx.x] = bits;
-            for (uint32_t rest = bits; rest; rest &= rest - 1) {
+            int k = rowstart[i];
+            for (uint32_t rest = rowbits[i]; rest; rest &= rest - 1, ++k) {
                 const int q = __ffs(rest) - 1;
-                const int64_t p2 = pos + q;
-                const uint32_t mw = __ldg(M.i8.mask + (p2 >> 5));
-                const uint32_t idx = __ldg(M.i8.base + (p2 >> 5)) + __popc(mw & ((1u << (p2 & 31)) - 1u));
-                cp_async16(hi_s + threadIdx.x * 16 + q, M.i8.hi + (int64_t)idx * 16);
-                sc_s[threadIdx.x * 16 + q] = 16.f * half_bits_to_float(__ldg(M.scales + p2) & 0x7FFFu);
+                const int bb = b + q;                       // bit position relative to word w
+                const int wi = bb >> 5;                     // 0 or 1
+                const uint32_t mw = msk[2 * i + wi];
+                const uint32_t idx = bas[2 * i + wi] + __popc(mw & ((1u << (bb & 31)) - 1u));
+                cp_async16(ent_hi + k, M.i8.hi + (int64_t)idx * 16);
+                ent_sc[k] = 16.f * half_bits_to_float(__ldg(M.scales + pos + q) & 0x7FFFu);
             }
         }
         cp_commit();
@@ -325,9 +383,11 @@ __device__ void int8_fix(const QView &M, int row0, int row_end, int col0, int nc
         __syncthreads();
         if (active) {
             for (int rr = sl; rr < nr; rr += slices) {
-                if (!((bits_s[rr] >> gi) & 1u)) continue;
-                const uint32_t hw = reinterpret_cast<const uint32_t *>(hi_s + rr * 16 + gi)[wsel];
-                const float s16 = sc_s[rr * 16 + gi];
+                const uint32_t bits = rowbits[rr];
+                if (!((bits >> gi) & 1u)) continue;
+                const int k = rowstart[rr] + __popc(bits & ((1u << gi) - 1u));
+                const uint32_t hw = reinterpret_cast<const uint32_t *>(ent_hi + k)[wsel];
+                const float s16 = ent_sc[k];
                 float xv[NT];
 #pragma unroll
                 for (int t = 0; t < NT; ++t) xv[t] = in_s[t * in_ld + (rc - row0 + rr)] * s16;
@@ -339,6 +399,7 @@ __device__ void int8_fix(const QView &M, int row0, int row_end, int col0, int nc
                 }
             }
         }
+        rc += nr;
     }
     __syncthreads();
     if (active) {
@@ -361,6 +422,7 @@ __device__ void int8_fix(const QView &M, int row0, int row_end, int col0, int nc
 struct Smem {
     float *lut;    // 32: NF4 levels, then the identity table 0..15
     uint8_t *stages;  // kStages * kStageBytes
+    uint8_t *i8s;     // kI8Scratch
     float *in_s;   // staged input vectors
     float *red_s;  // (kWarps+1) * 4 * max(r, kTileN)
     float *g_s;    // 4 * kTileN
@@ -384,11 +446,14 @@ __device__ __forceinline__ uint32_t cta_arrive(uint32_t *ctr, const Smem &S) {
 
 template <int LPR, int NT>
 __device__ __forceinline__ void in_chunk(const QView &M, bool has_i8, int row0, int row_end, int r, const float *in_s,
-                                         int kc, const Smem &S, float *part_rows, int ldo) {
+                                         int kc, const Smem &S, float *part_rows, int ldo, bool pre) {
     u64 acc[NT][8];
-    vecmat_staged<LPR, NT>(M, row0, row_end, 0, r, in_s, kc, S.lut, S.stages, acc);
+    if (pre)
+        vecmat_staged<LPR, NT, kLoop>(M, row0, row_end, 0, r, in_s, kc, S.lut, S.stages, acc);
+    else
+        vecmat_staged<LPR, NT>(M, row0, row_end, 0, r, in_s, kc, S.lut, S.stages, acc);
     float *res = cta_reduce<LPR, NT>(acc, r, S.red_s);
-    if (has_i8) int8_fix<NT>(M, row0, row_end, 0, r, in_s, kc, res, LPR * 16, S.red_s, S.stages);
+    if (has_i8) int8_fix<NT>(M, row0, row_end, 0, r, in_s, kc, res, LPR * 16, S.red_s, S.i8s);
 #pragma unroll
     for (int t = 0; t < NT; ++t)
         for (int col = threadIdx.x; col < r; col += kThreads) part_rows[(int64_t)t * ldo + col] = res[t * r + col];
@@ -401,11 +466,15 @@ __device__ void item_in(const DecodeArgs &a, const Smem &S, int ai, int m, int k
     const int kc = PH == 1 ? a.kc1 : a.kc2, ks = PH == 1 ? a.ks1 : a.ks2, r = a.r;
     const int e = a.rt.active[ai];
     const int p0 = a.rt.offsets[e], ne = a.rt.offsets[e + 1] - p0;
-    if (PH == 3) cta_wait(a.cnt2 + e, (uint32_t)a.nct_f, a, S);
     const latent_qmatrix &qm = PH == 1 ? (m == 0 ? a.gate_a : a.up_a) : a.down_a;
     const QView M = expert_view(qm, e);
     const bool has_i8 = expert_has_int8(qm, e);
     const int row0 = ksel * kc, row_end = min(M.rows, row0 + kc);
+    {   // start streaming the weights before waiting for inputs
+        u64 none[1][8];
+        vecmat_staged<LPR, 1, kPrologue>(M, row0, row_end, 0, r, nullptr, 0, S.lut, S.stages, none);
+    }
+    if (PH == 3) cta_wait(a.cnt2 + e, (uint32_t)a.nct_f, a, S);
     const int ldo = nmat * r;
     float *part = PH == 1 ? a.part1 : a.part2;
     for (int tc = 0; tc < ne; tc += 4) {
@@ -429,13 +498,13 @@ __device__ void item_in(const DecodeArgs &a, const Smem &S, int ai, int m, int k
         __syncthreads();
         float *rows = part + ((int64_t)ksel * a.R + p0 + tc) * ldo + m * r;
         if (nt == 1)
-            in_chunk<LPR, 1>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo);
+            in_chunk<LPR, 1>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo, tc == 0);
         else if (nt == 2)
-            in_chunk<LPR, 2>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo);
+            in_chunk<LPR, 2>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo, tc == 0);
         else if (nt == 3)
-            in_chunk<LPR, 3>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo);
+            in_chunk<LPR, 3>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo, tc == 0);
         else
-            in_chunk<LPR, 4>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo);
+            in_chunk<LPR, 4>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo, tc == 0);
     }
     uint32_t *arr = (PH == 1 ? a.arr1 : a.arr3) + e;
     if (cta_arrive(arr, S) != (uint32_t)(nmat * ks - 1)) return;
@@ -455,18 +524,25 @@ __device__ void item_in(const DecodeArgs &a, const Smem &S, int ai, int m, int k
 template <int NT>
 __device__ __forceinline__ void gateup_chunk(const DecodeArgs &a, const Smem &S, const QView &Mg, bool gi8,
                                              const QView &Mu, bool ui8, int col0, int ncols, int p,
-                                             const float *in_g, const float *in_u) {
+                                             const float *in_g, const float *in_u, bool pre) {
     constexpr int W = kTileN;
     const int r = a.r;
     u64 acc[NT][8];
-    vecmat_staged<16, NT>(Mg, 0, r, col0, ncols, in_g, r, S.lut, S.stages, acc);
+    if (pre)
+        vecmat_staged<16, NT, kLoop>(Mg, 0, r, col0, ncols, in_g, r, S.lut, S.stages, acc);
+    else
+        vecmat_staged<16, NT>(Mg, 0, r, col0, ncols, in_g, r, S.lut, S.stages, acc);
+    {   // the up matrix starts streaming while the gate sums are reduced
+        u64 none[1][8];
+        vecmat_staged<16, 1, kPrologue>(Mu, 0, r, col0, ncols, nullptr, 0, S.lut, S.stages, none);
+    }
     float *res = cta_reduce<16, NT>(acc, ncols, S.red_s);
-    if (gi8) int8_fix<NT>(Mg, 0, r, col0, ncols, in_g, r, res, W, S.red_s, S.stages);
+    if (gi8) int8_fix<NT>(Mg, 0, r, col0, ncols, in_g, r, res, W, S.red_s, S.i8s);
     for (int i = threadIdx.x; i < NT * W; i += kThreads) S.g_s[i] = res[i];
     __syncthreads();
-    vecmat_staged<16, NT>(Mu, 0, r, col0, ncols, in_u, r, S.lut, S.stages, acc);
+    vecmat_staged<16, NT, kLoop>(Mu, 0, r, col0, ncols, in_u, r, S.lut, S.stages, acc);
     res = cta_reduce<16, NT>(acc, ncols, S.red_s);
-    if (ui8) int8_fix<NT>(Mu, 0, r, col0, ncols, in_u, r, res, W, S.red_s, S.stages);
+    if (ui8) int8_fix<NT>(Mu, 0, r, col0, ncols, in_u, r, res, W, S.red_s, S.i8s);
     const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
     for (int i = threadIdx.x; i < NT * W; i += kThreads) {
         const int t = i / W, col = i - t * W;
@@ -482,10 +558,14 @@ __device__ void item_gateup(const DecodeArgs &a, const Smem &S, int ai, int ct) 
     const int r = a.r;
     const int e = a.rt.active[ai];
     const int p0 = a.rt.offsets[e], ne = a.rt.offsets[e + 1] - p0;
-    cta_wait(a.flag1 + e, 1u, a, S);
     const QView Mg = expert_view(a.gate_b, e), Mu = expert_view(a.up_b, e);
     const bool gi8 = expert_has_int8(a.gate_b, e), ui8 = expert_has_int8(a.up_b, e);
     const int col0 = ct * kTileN, ncols = min(kTileN, a.f - col0);
+    {
+        u64 none[1][8];
+        vecmat_staged<16, 1, kPrologue>(Mg, 0, r, col0, ncols, nullptr, 0, S.lut, S.stages, none);
+    }
+    cta_wait(a.flag1 + e, 1u, a, S);
     float *in_g = S.in_s, *in_u = S.in_s + 4 * r;
     for (int tc = 0; tc < ne; tc += 4) {
         const int nt = min(4, ne - tc);
@@ -500,25 +580,28 @@ __device__ void item_gateup(const DecodeArgs &a, const Smem &S, int ai, int ct) 
         __syncthreads();
         const int p = p0 + tc;
         if (nt == 1)
-            gateup_chunk<1>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u);
+            gateup_chunk<1>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u, tc == 0);
         else if (nt == 2)
-            gateup_chunk<2>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u);
+            gateup_chunk<2>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u, tc == 0);
         else if (nt == 3)
-            gateup_chunk<3>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u);
+            gateup_chunk<3>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u, tc == 0);
         else
-            gateup_chunk<4>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u);
+            gateup_chunk<4>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u, tc == 0);
     }
     cta_arrive(a.cnt2 + e, S);
 }
 
 template <int NT>
 __device__ __forceinline__ void down_chunk(const DecodeArgs &a, const Smem &S, const QView &M, bool i8, int col0,
-                                           int ncols, int p) {
+                                           int ncols, int p, bool pre) {
     constexpr int W = kTileN;
     u64 acc[NT][8];
-    vecmat_staged<16, NT>(M, 0, a.r, col0, ncols, S.in_s, a.r, S.lut, S.stages, acc);
+    if (pre)
+        vecmat_staged<16, NT, kLoop>(M, 0, a.r, col0, ncols, S.in_s, a.r, S.lut, S.stages, acc);
+    else
+        vecmat_staged<16, NT>(M, 0, a.r, col0, ncols, S.in_s, a.r, S.lut, S.stages, acc);
     float *res = cta_reduce<16, NT>(acc, ncols, S.red_s);
-    if (i8) int8_fix<NT>(M, 0, a.r, col0, ncols, S.in_s, a.r, res, W, S.red_s, S.stages);
+    if (i8) int8_fix<NT>(M, 0, a.r, col0, ncols, S.in_s, a.r, res, W, S.red_s, S.i8s);
     const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
     for (int i = threadIdx.x; i < NT * W; i += kThreads) {
         const int t = i / W, col = i - t * W;
@@ -542,10 +625,14 @@ __device__ void item_down(const DecodeArgs &a, const Smem &S, int ai, int ct) {
     const int r = a.r;
     const int e = a.rt.active[ai];
     const int p0 = a.rt.offsets[e], ne = a.rt.offsets[e + 1] - p0;
-    cta_wait(a.flag3 + e, 1u, a, S);
     const QView M = expert_view(a.down_b, e);
     const bool i8 = expert_has_int8(a.down_b, e);
     const int col0 = ct * kTileN, ncols = min(kTileN, a.d - col0);
+    {
+        u64 none[1][8];
+        vecmat_staged<16, 1, kPrologue>(M, 0, r, col0, ncols, nullptr, 0, S.lut, S.stages, none);
+    }
+    cta_wait(a.flag3 + e, 1u, a, S);
     for (int tc = 0; tc < ne; tc += 4) {
         const int nt = min(4, ne - tc);
         __syncthreads();
@@ -555,13 +642,13 @@ __device__ void item_down(const DecodeArgs &a, const Smem &S, int ai, int ct) {
         __syncthreads();
         const int p = p0 + tc;
         if (nt == 1)
-            down_chunk<1>(a, S, M, i8, col0, ncols, p);
+            down_chunk<1>(a, S, M, i8, col0, ncols, p, tc == 0);
         else if (nt == 2)
-            down_chunk<2>(a, S, M, i8, col0, ncols, p);
+            down_chunk<2>(a, S, M, i8, col0, ncols, p, tc == 0);
         else if (nt == 3)
-            down_chunk<3>(a, S, M, i8, col0, ncols, p);
+            down_chunk<3>(a, S, M, i8, col0, ncols, p, tc == 0);
         else
-            down_chunk<4>(a, S, M, i8, col0, ncols, p);
+            down_chunk<4>(a, S, M, i8, col0, ncols, p, tc == 0);
     }
     if (a.flags & LATENT_FLAG_OUT_PER_SLOT) return;
     __threadfence();
@@ -607,7 +694,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode(DecodeArgs a) {
     Smem S;
     S.lut = s_lut;
     S.stages = sm_raw;
-    float *sm = reinterpret_cast<float *>(sm_raw + kStages * kStageBytes);
+    S.i8s = sm_raw + kStages * kStageBytes;
+    float *sm = reinterpret_cast<float *>(sm_raw + kStages * kStageBytes + kI8Scratch);
     S.in_s = sm;
     S.red_s = sm + a.in_floats;
     S.g_s = S.red_s + a.red_floats;
@@ -662,7 +750,7 @@ void plan_split(int K, int r, int &kc, int &ks) {
     const int step = kWarps * (32 / lpr);
     int rows = 32768 / (r / 2);
     rows = rows < step ? step : rows;
-    rows = rows > 1024 ? 1024 : rows;
+    rows = rows > 512 ? 512 : rows;
     kc = round_up(rows, 64);
     if (kc > round_up(K, 64)) kc = round_up(K, 64);
     ks = (K + kc - 1) / kc;
@@ -715,7 +803,8 @@ size_t decode_scratch_floats(const DecodeArgs &a) {
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t s, Marks *marks) {
     const void *fn = pick_decode_fn(a.r, a.x_type);
     if (!fn) return cudaErrorInvalidValue;
-    const size_t smem = (size_t)kStages * kStageBytes + (size_t)(a.in_floats + a.red_floats + 4 * kTileN) * sizeof(float);
+    const size_t smem = (size_t)kStages * kStageBytes + kI8Scratch +
+                        (size_t)(a.in_floats + a.red_floats + 4 * kTileN) * sizeof(float);
     cudaError_t err = ensure_smem(fn, smem);
     if (err != cudaSuccess) return err;
     int dev = 0, sms = 0, per_sm = 0;

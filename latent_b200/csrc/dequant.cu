@@ -9,6 +9,9 @@ namespace {
 // level[code] * float(scale) (NF4, loader/latent_loader.py:144) or
 // float(int8) * float(scale) (INT8, :169) -- a single fp32 rounding.
 __global__ void __launch_bounds__(256) k_dequant(latent_qmatrix m, int expert, float *out) {
+    __shared__ float lut[16];
+    if (threadIdx.x < 16) lut[threadIdx.x] = kNF4Levels[threadIdx.x];
+    __syncthreads();
     const QView M = expert_view(m, expert);
     const int64_t n = (int64_t)M.rows * M.cols;
     const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
@@ -25,7 +28,7 @@ __global__ void __launch_bounds__(256) k_dequant(latent_qmatrix m, int expert, f
         for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(int8_elem(w, hw, j), sc);
     } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(kNF4Levels[(w >> (4 * j)) & 15u], sc);
+        for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(lut[(w >> (4 * j)) & 15u], sc);
     }
     float4 *dst = reinterpret_cast<float4 *>(out + i);
     dst[0] = make_float4(v[0], v[1], v[2], v[3]);

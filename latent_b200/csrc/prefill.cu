@@ -41,6 +41,9 @@ constexpr int kBK = 64;   // K per stage (128 bytes of f16: one swizzle atom)
 __global__ void __launch_bounds__(256) k_pf_dequant_t(latent_qmatrix m, __half *dst, int64_t dst_expert_stride,
                                                        int row_off) {
     __shared__ float tile[64][65];
+    __shared__ float lut[16];  // per-thread table indices: shared memory, not the constant cache
+    if (threadIdx.x < 16) lut[threadIdx.x] = kNF4Levels[threadIdx.x];
+    __syncthreads();
     const int e = blockIdx.z;
     const QView M = expert_view(m, e);
     const int K = M.rows, N = M.cols;
@@ -65,8 +68,8 @@ __global__ void __launch_bounds__(256) k_pf_dequant_t(latent_qmatrix m, __half *
             } else {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    tile[kk][nn + j] = __fmul_rn(kNF4Levels[(q.x >> (4 * j)) & 15u], sc);
-                    tile[kk][nn + 8 + j] = __fmul_rn(kNF4Levels[(q.y >> (4 * j)) & 15u], sc);
+                    tile[kk][nn + j] = __fmul_rn(lut[(q.x >> (4 * j)) & 15u], sc);
+                    tile[kk][nn + 8 + j] = __fmul_rn(lut[(q.y >> (4 * j)) & 15u], sc);
                 }
             }
         }
@@ -342,7 +345,7 @@ __global__ void __launch_bounds__(256, 1) k_pf_gemm(const __grid_constant__ CUte
 #pragma unroll
                             for (int t = 0; t < 8; ++t) {
                                 const float gg = __uint_as_float(v[j + t]), uu = __uint_as_float(u[j + t]);
-                                hv[t] = __float2half_rn(silu_f32(gg) * uu * wrow);
+                                hv[t] = __float2half_rn(silu_fast(gg) * uu * wrow);
                             }
                             if (n0 + c + j + 8 <= g.N) *reinterpret_cast<uint4 *>(o + j) = *reinterpret_cast<uint4 *>(hv);
                         }
