@@ -14,28 +14,36 @@
  * Factor storage ("stacked" layout, one tensor per factor kind, all experts
  * contiguous -- the per-expert stacking of the reference GGUF writer,
  * loader/write_latent_gguf.py:101-123 and 230-255, with the nibble packing
- * it actually writes):
- *   codes   uint8  [n_expert][rows][cols/2]   two 4-bit codes per byte, the
- *                                              even column in the low nibble
+ * it actually writes).  Each expert matrix [rows][cols] is a sequence of
+ * 32-element groups in 256-column tile-major order: tile c (columns
+ * 256c .. min(cols, 256c+256)-1) stores its rows one after another, each row
+ * its ng_c = min(8, cols/32 - 8c) groups.  Group (row, col) has the
+ * expert-local flat index
+ *     q = c*rows*8 + row*ng_c + (col - 256c)/32,    c = col/256,
+ * so a matrix of at most 256 columns is plain row-major.
+ *   codes   uint8  [n_expert][rows*cols/32][16] group q at byte 16q: two 4-bit
+ *                                              codes per byte, the even column
+ *                                              in the low nibble
  *                                              (loader/latent_loader.py:129)
- *   scales  fp16   [n_expert][rows][cols/32]  one scale per 32-element group
- *                                              along a row; scales are >= 0,
- *                                              and the sign bit flags an
- *                                              INT8 group
+ *   scales  fp16   [n_expert][rows*cols/32]   scale of group q; scales are
+ *                                              >= 0 and the sign bit flags
+ *                                              an INT8 group
  *   NF4 group:  value = NF4_LEVEL[code] * float(scale)
  *   INT8 group: value = float(int8(hi << 4 | lo)) * float(|scale|), where lo
  *               is the 4-bit code in `codes` and hi comes from `i8_hi`.
- *   i8_mask uint32 [n_expert][mask_words]     bit g%32 of word g/32 set when
- *                                              expert-local group g (= row *
- *                                              cols/32 + col/32) is INT8;
+ *   i8_mask uint32 [n_expert][mask_words]     bit q%32 of word q/32 set when
+ *                                              group q is INT8;
  *                                              mask_words = ceil(rows*cols/1024)
  *   i8_base uint32 [n_expert][mask_words]     number of INT8 groups in the
  *                                              whole tensor before word w
- *   i8_hi   uint8  [n_int8_groups][16]        high nibbles, same nibble order
- * i8_mask/i8_base/i8_hi are NULL when no group is INT8.
- * cols must be a multiple of 32 and rows*cols/2 bytes per expert; the rank
- * dimension may be zero-padded (code 7 = 0.0, scale 1.0), which leaves every
- * result unchanged.
+ *   i8_hi   uint8  [n_int8_groups][16]        high nibbles of the INT8
+ *                                              groups in (expert, q) order,
+ *                                              same nibble order as codes
+ * i8_mask/i8_base/i8_hi are NULL when no group is INT8.  The tile order lets
+ * a kernel streaming a row range of one column tile read its codes, scales
+ * and INT8 records as three contiguous runs (latent_b200/format.py packs it).
+ * cols must be a multiple of 32; the rank dimension may be zero-padded
+ * (code 7 = 0.0, scale 1.0), which leaves every result unchanged.
  */
 #ifndef LATENT_FFN_H
 #define LATENT_FFN_H
@@ -56,7 +64,7 @@ struct CUevent_st;  /* cudaEvent_t */
 #define LATENT_API
 #endif
 
-#define LATENT_ABI_VERSION 1
+#define LATENT_ABI_VERSION 2
 
 typedef enum latent_status {
     LATENT_OK = 0,

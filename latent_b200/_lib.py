@@ -132,7 +132,7 @@ def lib() -> C.CDLL:
                 fn = getattr(h, name)
                 fn.restype = res
                 fn.argtypes = args
-            if h.latent_abi_version() != 1:
+            if h.latent_abi_version() != 2:
                 raise RuntimeError("liblatent_b200.so ABI version mismatch")
             _lib = h
     return _lib

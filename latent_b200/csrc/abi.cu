@@ -30,7 +30,7 @@ constexpr size_t kAlign = 256;
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct Layout {
-    size_t err, counts, offsets, active, n_active, sem, order, pos, block_counts, scratch, total;
+    size_t err, counts, offsets, active, n_active, sem, order, pos, block_counts, virt, n_virt, vslot, scratch, total;
     int n_sem;
 };
 
@@ -40,7 +40,7 @@ int check_qmatrix(const latent_qmatrix &m, int64_t rows, int64_t cols, bool need
     if (m.rows != rows || m.cols != cols) return LATENT_ERR_SHAPE;
     if (!need_ptrs) return LATENT_OK;
     if (!m.codes || !m.scales) return LATENT_ERR_INVALID;
-    if (!aligned(m.codes, 16) || !aligned(m.scales, 4)) return LATENT_ERR_ALIGN;
+    if (!aligned(m.codes, 16) || !aligned(m.scales, 16)) return LATENT_ERR_ALIGN;
     const bool any = m.i8_mask || m.i8_base || m.i8_hi;
     if (any && !(m.i8_mask && m.i8_base && m.i8_hi)) return LATENT_ERR_INVALID;
     if (m.i8_hi && !aligned(m.i8_hi, 16)) return LATENT_ERR_ALIGN;
@@ -128,6 +128,10 @@ Layout layout(const latent_ffn_desc *d, const DecodeArgs &a, int path) {
     L.order = o;         o = align_up(o + R * 4);
     L.pos = o;           o = align_up(o + R * 4);
     L.block_counts = o;  o = align_up(o + route_block_counts_bytes((int)E, (int)R));
+    const bool dec = path != LATENT_PATH_PREFILL;
+    L.virt = o;          o = align_up(o + (dec ? (size_t)a.n_virt_max * 16 : 0));
+    L.n_virt = o;        o = align_up(o + (dec ? 4 : 0));
+    L.vslot = o;         o = align_up(o + (dec ? R * 4 : 0));
     L.scratch = o;
     o = align_up(o + (path == LATENT_PATH_PREFILL ? prefill_scratch_bytes(a) : decode_scratch_floats(a) * sizeof(float)));
     L.total = o;
@@ -203,6 +207,11 @@ int forward_impl(const latent_ffn_desc *desc, CUstream_st *stream, Marks *marks)
     ra.order = at<int32_t>(ws, L.order);
     ra.pos = at<int32_t>(ws, L.pos);
     ra.block_counts = at<int32_t>(ws, L.block_counts);
+    if (path != LATENT_PATH_PREFILL) {
+        ra.virt = at<int4>(ws, L.virt);
+        ra.n_virt = at<int32_t>(ws, L.n_virt);
+        ra.vslot = at<int32_t>(ws, L.vslot);
+    }
     if (marks) marks->mark(s);
     if ((st = cuda_status(launch_route(ra, s)))) return st;
     if (marks) marks->mark(s);
@@ -216,22 +225,11 @@ int forward_impl(const latent_ffn_desc *desc, CUstream_st *stream, Marks *marks)
     a.rt.sem = ra.sem;
     a.rt.err = ra.err;
     if (path == LATENT_PATH_PREFILL) return cuda_status(launch_prefill(a, at<void>(ws, L.scratch), s, marks));
-    float *f = at<float>(ws, L.scratch);
-    const size_t R = (size_t)a.R, r = (size_t)a.r;
-    a.part1 = f;  f += (size_t)a.ks1 * R * 2 * r;
-    a.t = f;      f += R * 2 * r;
-    a.h = f;      f += R * (size_t)a.f;
-    a.part2 = f;  f += (size_t)a.ks2 * R * r;
-    a.s = f;      f += R * r;
-    a.y = f;
-    uint32_t *sem = ra.sem;
-    a.work = sem;       sem += 1;
-    a.arr1 = sem;       sem += a.E;
-    a.flag1 = sem;      sem += a.E;
-    a.cnt2 = sem;       sem += a.E;
-    a.arr3 = sem;       sem += a.E;
-    a.flag3 = sem;      sem += a.E;
-    a.tokcnt = sem;
+    a.rt.virt = ra.virt;
+    a.rt.n_virt = ra.n_virt;
+    a.rt.vslot = ra.vslot;
+    decode_bind_scratch(a, at<float>(ws, L.scratch));
+    decode_bind_sem(a, ra.sem);
     return cuda_status(launch_decode(a, s, marks));
 }
 
@@ -260,6 +258,7 @@ extern "C" LATENT_API int latent_expert_ffn_check(const latent_ffn_desc *desc, C
         return LATENT_ERR_CUDA;
     if (err & kErrExpertId) return LATENT_ERR_EXPERT_ID;
     if (err & kErrTimeout) return LATENT_ERR_TIMEOUT;
+    if (err & kErrLayout) return LATENT_ERR_UNSUPPORTED;
     return LATENT_OK;
 }
 

@@ -14,6 +14,7 @@ namespace latent {
 enum : uint32_t {
     kErrExpertId = 1u << 0,
     kErrTimeout = 1u << 1,
+    kErrLayout = 1u << 2,  // a kernel's shared-memory layout assumption did not hold
 };
 
 // NF4 levels in code order.  Must equal the reference table
@@ -88,6 +89,16 @@ struct Int8Side {
         return true;
     }
 };
+
+// Flat group index of element (row, col) of a [rows][cols] factor in the
+// 256-column tile-major device order: tile c = col/256 holds its rows in
+// turn, each row its min(8, cols/32 - 8c) groups.  The index addresses the
+// 16 code bytes (codes + 16*q), the fp16 scale (scales[q]) and the INT8 bit.
+__device__ __forceinline__ int64_t tile_group(int rows, int cols, int row, int col) {
+    const int c = col >> 8;
+    const int ng = min(8, (cols >> 5) - 8 * c);
+    return (int64_t)c * rows * 8 + (int64_t)row * ng + ((col & 255) >> 5);
+}
 
 // Expert-local view of one stacked factor.
 struct QView {

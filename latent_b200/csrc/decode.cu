@@ -2,72 +2,158 @@
 // products on CUDA cores with fp32 accumulation (rel-L2 <= 1e-5 vs the fp32
 // reference runtime, loader/latent_runtime.py:35-59).
 //
-// One persistent, cooperatively launched kernel runs the whole chain.  Work
-// items are handed out in phase order by an atomic counter:
-//   phase 1  t = x . [A_g | A_u]   item = (expert, matrix, row chunk of d)  split-K
-//   phase 2  h = silu(t_g.B_g) * (t_u.B_u) [* w]   item = (expert, 256-column tile of f)
-//   phase 3  s = h . A_d           item = (expert, row chunk of f)          split-K
-//   phase 4  y = s . B_d           item = (expert, 256-column tile of d), fused top-k combine
-// An item waits (bounded) only for its own expert's previous phase:
-// phase-1/3 partial sums are reduced in chunk order by the last item to
-// arrive (arrival counter), which then publishes a ready flag; phase 3 waits
-// for all phase-2 tiles of its expert; the last phase-4 tile to finish a
-// (token, column tile) sums that token's top-k rows in slot order.  Items are
-// handed out in phase order and every CTA is resident (cooperative launch),
-// so every wait ends; a wait that exceeds its bound sets kErrTimeout and the
-// kernel runs to completion without waiting further.  Results are bitwise
-// deterministic.
+// One persistent, cooperatively launched kernel (one CTA per SM) streams the
+// whole chain.  Routed positions are grouped into virtual experts (an expert
+// and up to 8 of its consecutive routed positions).  For every virtual expert
+// the chain is four phases of "segments", a segment being one 256-column tile
+// of one factor matrix over all of its rows:
+//   phase 1  t = x . [A_g | A_u]        segments (matrix, tile of r), rows d
+//   phase 2  g|u = t . B_{g|u}          segments (tile of f, matrix), rows r
+//   phase 3  s = h . A_d, h = silu(g)u  segments (tile of r),         rows f
+//   phase 4  y = s . B_d                segments (tile of d),         rows r
+// followed by the top-k combine of y into out (phase 5).
 //
-// Inner loop: codes and scales stream through a 4-deep cp.async ring in
-// shared memory (memory parallelism independent of registers).  A lane owns
-// 16 consecutive columns of a row (8 code bytes, half a 32-element scale
-// group), turns codes into table byte offsets with one shift and one
-// and-or per 8 codes, looks each value up in a shared table and accumulates
-// x*scale*value with packed fp32x2 FMAs on 64-bit accumulators.  The table
-// has the 16 NF4 levels in banks 0-15 and the identity 0..15 in banks 16-31;
-// the sign bit of a group's scale (set for INT8 groups) selects the second,
-// so a warp lookup is one wavefront and INT8 groups cost the hot loop nothing
-// extra.  The INT8 high nibbles are added afterwards to the CTA's reduced
-// tile (int8_fix), in a fixed order.
+// Work partition: the segments of a phase, in order, form one stream of
+// 8-row blocks weighted by their width; each warp of the grid takes one
+// contiguous, equally weighted range of it (no work queue, no CTA-wide
+// synchronisation).  A warp's range covers parts ("pieces") of one or a few
+// segments.  A piece accumulates its rows in registers, writes the partial
+// sums of its columns to a slot of its own and counts itself in on the
+// segment's arrival counter; the piece that completes the count adds all
+// partials of the segment in piece order (bitwise deterministic), applies the
+// phase epilogue (SwiGLU and the optional router weight after phase 2) and
+// sets the segment's ready flag.  A piece of the next phase waits (bounded)
+// for the ready flags of the segments it reads.  Every CTA is resident
+// (cooperative launch) and every warp takes its ranges in phase order, so
+// every wait ends; a wait that exceeds its bound sets kErrTimeout and the
+// kernel runs to completion without waiting further.
+//
+// Memory path: each warp streams its codes and scales through a private
+// 3-deep cp.async ring of 16-row stages (2 KB of codes + 256 B of scales at
+// full width), issued from per-piece pointers two stages ahead across piece
+// and phase boundaries, so the weight stream never waits for a dependency.
+// Inputs and INT8 records of the next stage are prefetched into registers.
+//
+// Inner loop: a lane owns 16 consecutive columns (8 code bytes) of a row when
+// the virtual expert has at most 4 tokens, else 8 columns.  One PRMT builds
+// the shared-memory address of a code byte's entry in a 64 KB table of float
+// pairs (16 replicas x 256 byte values x 2 tables, replica = lane % 16, so a
+// warp lookup touches every bank exactly twice) and one 64-bit load returns
+// the two decoded values, which feed packed fp32x2 FMAs directly.  Table 0
+// holds NF4 level pairs; table 1 holds (lo - 8, hi - 8) pairs and is selected
+// by the sign bit of the group's scale, which flags INT8 groups.
+//
+// INT8 groups: int8(hi:lo) = (lo - 8) + 16 * (hi' - 8) + 8 with hi' = hi ^ 8.
+// The main loop adds (lo - 8) through table 1.  After each stage the warp
+// walks the stage's INT8 records (one contiguous run in the tile-major order;
+// a lane takes its share of the rows of its own group) and adds
+// 16 * (hi' - 8) + 8 through the same table.
 #include "internal.h"
 
 namespace latent {
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kTileN = 256;  // output columns per tile on the output side
+typedef unsigned long long u64;
+
+#ifndef LATENT_DECODE_WARPS
+#define LATENT_DECODE_WARPS 12
+#endif
+constexpr int kSW = LATENT_DECODE_WARPS;                 // warps per CTA
+constexpr int kSThreads = kSW * 32;
+constexpr int kMaxCtas = 160;           // grid cap the workspace is sized for
+constexpr int kRing = 3;                // stages per warp ring (two issued ahead)
+constexpr int kStRows = 16;             // rows per stage
+constexpr int kStCode = kStRows * 128;  // code bytes per stage (at most)
+constexpr int kStScale = kStRows * 16;  // scale bytes per stage (at most)
+constexpr int kStBytes = kStCode + kStScale;
+constexpr int kRecStage = 32;           // INT8 records per stage staged in shared memory
+constexpr int kNT = kVirtTokens;        // tokens per virtual expert (8)
+constexpr int kMinUnits = 64;           // least work per warp, in (8 rows x 32 columns) units
 constexpr unsigned long long kWaitNs = 2000000000ull;  // a dependency wait gives up after 2 s
 
-typedef unsigned long long u64;
+// Per-warp shared memory (byte offsets); "x2" areas alternate by stage parity
+// because a stage's INT8 pass runs after the next stage's main loop.
+constexpr int kWRing = 0;
+constexpr int kWIn = kWRing + kRing * kStBytes;   // x2 float [kStRows][kNT] inputs of the stage
+constexpr int kWStash = kWIn + 2 * kStRows * kNT * 4;  // x2 uint16 [kStRows][8] scales of INT8 groups
+constexpr int kWRow = kWStash + 2 * kStRows * 8 * 2;   // x2 uint16 [kStRows] INT8 prefix | flags << 8
+constexpr int kWRec = kWRow + 2 * kStRows * 2;    // x2 uint8 [kRecStage][16] INT8 records of the stage
+constexpr int kWMeta = kWRec + 2 * kRecStage * 16;  // 4 x uint32 [4] INT8 table words of upcoming pieces
+constexpr int kWTok = kWMeta + 4 * 16;            // int [kNT] token rows of the piece (phase 1)
+constexpr int kWIter = kWTok + kNT * 4;           // Iter of the consumer
+constexpr int kWIssue = kWIter + 48;              // Iter of the stage issuer
+constexpr int kWarpBytes = kWIssue + 48;
+static_assert(kWarpBytes % 16 == 0, "warp area alignment");
+// CTA area at the start of dynamic shared memory, then the areas of the low
+// warps, the pair table at shared address 64 K, the remaining warps after it.
+constexpr int kCtaBytes = 512;
+constexpr uint32_t kTableAddr = 65536;
+constexpr int kTableBytes = 65536;
+constexpr int kMaxSmemBase = 4096;      // dynamic shared memory must start below this address
+constexpr int kLowWarpsFit = (int)((kTableAddr - kMaxSmemBase - kCtaBytes) / kWarpBytes);
+constexpr int kLowWarps = kLowWarpsFit < kSW ? kLowWarpsFit : kSW;
+constexpr int kDynSmem = (int)kTableAddr + kTableBytes + (kSW - kLowWarps) * kWarpBytes;
+static_assert(kDynSmem <= 227 * 1024, "shared memory budget");
 
 __device__ __forceinline__ u64 pack2(float a, float b) {
     u64 r;
-    asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
     return r;
 }
-
 __device__ __forceinline__ void unpack2(u64 v, float &a, float &b) {
-    asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
 }
-
 __device__ __forceinline__ void ffma2(u64 &acc, u64 x, u64 v) {
     asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(x), "l"(v));
 }
-
-__device__ __forceinline__ float lut_at(const float *lut, uint32_t byte_off) {
-    return *reinterpret_cast<const float *>(reinterpret_cast<const char *>(lut) + byte_off);
+__device__ __forceinline__ u64 fadd2(u64 a, u64 b) {
+    u64 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ u64 lds64(uint32_t addr) {
+    u64 v;
+    asm("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint2 lds_v2(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t addr) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void cp_async16(uint32_t s, const void *g) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
-__device__ __forceinline__ uint32_t byte_of(uint32_t w, int b) { return __byte_perm(w, 0u, 0x4440u | b); }
-
-// Bounded wait until *flag >= target (thread 0 of the CTA only).  Returns
-// false (and records kErrTimeout) when the bound is exceeded or another CTA
-// already gave up.
+// Bounded wait until *flag >= target (one lane).  Returns false (and records
+// kErrTimeout) when the bound is exceeded or another warp already gave up.
 __device__ bool wait_ge(const uint32_t *flag, uint32_t target, uint32_t *err) {
-    unsigned long long t0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    const unsigned long long t0 = gtime();
     unsigned ns = 32;
     while (true) {
         uint32_t v;
@@ -76,704 +162,869 @@ __device__ bool wait_ge(const uint32_t *flag, uint32_t target, uint32_t *err) {
         uint32_t e;
         asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(e) : "l"(err) : "memory");
         if (e & kErrTimeout) return false;
-        unsigned long long now;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-        if (now - t0 > kWaitNs) {
+        if (gtime() - t0 > kWaitNs) {
             atomicOr(err, kErrTimeout);
             return false;
         }
         __nanosleep(ns);
-        if (ns < 1024) ns <<= 1;
+        if (ns < 256) ns <<= 1;
     }
 }
 
-// cp.async (LDGSTS) helpers.
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void cp_async16(void *s, const void *g) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(s)), "l"(g) : "memory");
-}
-__device__ __forceinline__ void cp_async4(void *s, const void *g) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(s)), "l"(g) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-constexpr int kStages = 4;
-constexpr int kWarpStageCode = 1024;  // code bytes per warp per stage
-constexpr int kWarpStageScale = 256;  // scale bytes per warp per stage
-constexpr int kWarpStageBytes = kWarpStageCode + kWarpStageScale;
-constexpr int kWarpRing = kStages * kWarpStageBytes;
-constexpr int kStageBytes = kWarps * kWarpRing / kStages;  // per-CTA bytes of one stage (all warps)
-
-// One staged row of a lane's 16 columns: acc[t][p] (columns 2p, 2p+1) += in[t]*scale*table[code].
-// `tsel` adds 64 bytes to every table offset: the identity table that decodes
-// the low nibble of an INT8 group (its high nibble is added by int8_fix).
-template <int NT>
-__device__ __forceinline__ void row_fma(uint2 q, uint32_t tsel, float sc, const float *xin, int xstride,
-                                        const float *lut, u64 (&acc)[NT][8]) {
-    u64 xs[NT];
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-        const float v = xin[t * xstride] * sc;
-        xs[t] = pack2(v, v);
-    }
-#pragma unroll
-    for (int w2 = 0; w2 < 2; ++w2) {
-        const uint32_t word = w2 ? q.y : q.x;
-        const uint32_t e4 = ((word << 2) & 0x3C3C3C3Cu) | tsel;  // even columns: table byte offsets
-        const uint32_t o4 = ((word >> 2) & 0x3C3C3C3Cu) | tsel;  // odd columns
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const u64 vv = pack2(lut_at(lut, byte_of(e4, j)), lut_at(lut, byte_of(o4, j)));
-#pragma unroll
-            for (int t = 0; t < NT; ++t) ffma2(acc[t][4 * w2 + j], xs[t], vv);
-        }
-    }
+// INT8 records of expert e before its flat group q (q may be one past the end).
+__device__ __forceinline__ uint32_t int8_before(const latent_qmatrix &m, int e, int64_t q) {
+    const int64_t groups = m.rows * m.cols / 32, words = (groups + 31) / 32;
+    const uint32_t *mask = m.i8_mask + (int64_t)e * words, *base = m.i8_base + (int64_t)e * words;
+    if (q >= groups) return __ldg(base + words - 1) + __popc(__ldg(mask + words - 1));
+    const int64_t w = q >> 5;
+    return __ldg(base + w) + __popc(__ldg(mask + w) & ((1u << (q & 31)) - 1u));
 }
 
-// Accumulates rows [row0, row_end) x columns [col0, col0+ncols) of M against
-// in_s[t * in_ld + (row - row0)] into the calling lane's 16-column slice.
-// Each warp streams its own contiguous share of the rows through a private
-// kStages-deep cp.async ring in `stages` (kWarpRing bytes per warp), so the
-// loop synchronises only within the warp.  LPR lanes span a row (16 columns
-// each), 32/LPR rows per warp step.  All threads of the CTA must call it.
-// phase: kFull (prologue + loop), kPrologue (issue the first kStages-1
-// stages and return: lets an item start streaming weights before it waits for
-// its inputs), kLoop (the rest; the same geometry's prologue was issued).
-enum : int { kFull = 0, kPrologue = 1, kLoop = 2 };
-
-template <int LPR, int NT, int PHASE = kFull>
-__device__ __forceinline__ void vecmat_staged(const QView &M, int row0, int row_end, int col0, int ncols,
-                                              const float *in_s, int in_ld, const float *lut, uint8_t *stages,
-                                              u64 (&acc)[NT][8]) {
-    constexpr int RPW = 32 / LPR;
-#pragma unroll
-    for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[t][j] = 0ull;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int cb = ncols >> 1, ng = ncols >> 5;
-    const int spitch = (ng * 2 + 3) & ~3;
-    // this warp's rows: a multiple of RPW
-    const int nrows = row_end - row0;
-    const int per = (nrows + kWarps * RPW - 1) / (kWarps * RPW) * RPW;
-    const int wr0 = row0 + warp * per, wr1 = min(row_end, wr0 + per);
-    uint8_t *ring = stages + warp * kWarpRing;
-    int SR = kWarpStageCode / cb;
-    if (SR * spitch > kWarpStageScale) SR = kWarpStageScale / spitch;
-    SR = SR / RPW * RPW;
-    const int nst = wr1 > wr0 ? (wr1 - wr0 + SR - 1) / SR : 0;
-    const int64_t rb = M.cols >> 1, gpr = M.cols >> 5;
-    const bool sc4 = ((gpr | ng | (col0 >> 5)) & 1) == 0;
-    const int chunks = cb >> 4;
-    const int cshift = (chunks & (chunks - 1)) == 0 ? __ffs(chunks) - 1 : -1;
-    const int n4 = ng >> 1;
-    const int sshift = (n4 & (n4 - 1)) == 0 && n4 > 0 ? __ffs(n4) - 1 : -1;
-    const uint8_t *gcodes = M.codes + (col0 >> 1);
-    const uint16_t *gscales = M.scales + (col0 >> 5);
-
-    auto issue = [&](int s) {
-        if (s < nst) {
-            uint8_t *buf = ring + (s % kStages) * kWarpStageBytes;
-            const int rbase = wr0 + s * SR;
-            const int nr = min(SR, wr1 - rbase);
-            for (int i = lane; i < nr * chunks; i += 32) {
-                const int rr = cshift >= 0 ? i >> cshift : i / chunks;
-                const int ch = i - rr * chunks;
-                cp_async16(buf + rr * cb + ch * 16, gcodes + (int64_t)(rbase + rr) * rb + ch * 16);
-            }
-            uint8_t *sbuf = buf + kWarpStageCode;
-            if (sc4) {
-                for (int i = lane; i < nr * n4; i += 32) {
-                    const int rr = sshift >= 0 ? i >> sshift : i / n4;
-                    const int ch = i - rr * n4;
-                    cp_async4(sbuf + rr * spitch + ch * 4, gscales + (int64_t)(rbase + rr) * gpr + ch * 2);
-                }
-            } else {
-                for (int i = lane; i < nr * ng; i += 32) {
-                    const int rr = i / ng, gi = i - rr * ng;
-                    *reinterpret_cast<uint16_t *>(sbuf + rr * spitch + gi * 2) =
-                        __ldg(gscales + (int64_t)(rbase + rr) * gpr + gi);
-                }
-            }
-        }
-        cp_commit();
-    };
-
-    if (PHASE != kLoop)
-        for (int s = 0; s < kStages - 1; ++s) issue(s);
-    if (PHASE == kPrologue) return;
-    const int cl = (lane % LPR) * 16;
-    const int rs = lane / LPR;
-    for (int s = 0; s < nst; ++s) {
-        cp_wait<kStages - 2>();
-        __syncwarp();
-        issue(s + kStages - 1);
-        if (cl < ncols) {
-            const uint8_t *buf = ring + (s % kStages) * kWarpStageBytes;
-            const uint8_t *sbuf = buf + kWarpStageCode;
-            const int rbase = wr0 + s * SR;
-            const int nr = min(SR, wr1 - rbase);
-            const float *xin = in_s + (rbase - row0);
-            for (int rr = rs; rr < nr; rr += RPW) {
-                const uint2 q = *reinterpret_cast<const uint2 *>(buf + rr * cb + (cl >> 1));
-                const uint16_t sb = *reinterpret_cast<const uint16_t *>(sbuf + rr * spitch + (cl >> 5) * 2);
-                const uint32_t tsel = (sb & 0x8000u) ? 0x40404040u : 0u;
-                row_fma<NT>(q, tsel, half_bits_to_float(sb & 0x7FFFu), xin + rr, in_ld, lut, acc);
-            }
-        }
-        __syncwarp();
-    }
-    cp_wait<0>();
-    __syncthreads();
-}
-
-// Sums lanes that share columns (the 32/LPR row lanes of a warp, then the
-// warps through red_s[kWarps][NT][W], W = LPR*16).  The CTA's sums end up at
-// red_s + kWarps*NT*W, indexed t*W + col.
-template <int LPR, int NT>
-__device__ __forceinline__ float *cta_reduce(u64 (&acc)[NT][8], int ncols, float *red_s) {
-    constexpr int W = LPR * 16;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float a[NT][16];
-#pragma unroll
-    for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int p = 0; p < 8; ++p) unpack2(acc[t][p], a[t][2 * p], a[t][2 * p + 1]);
-#pragma unroll
-    for (int o = LPR; o < 32; o <<= 1)
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-#pragma unroll
-            for (int j = 0; j < 16; ++j) a[t][j] += __shfl_xor_sync(0xffffffffu, a[t][j], o);
-    const int cl = lane * 16;
-    if (lane < LPR && cl < ncols) {
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            float4 *dst = reinterpret_cast<float4 *>(red_s + (warp * NT + t) * W + cl);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) dst[j] = make_float4(a[t][4 * j], a[t][4 * j + 1], a[t][4 * j + 2], a[t][4 * j + 3]);
-        }
-    }
-    __syncthreads();
-    float *res = red_s + kWarps * NT * W;
-    for (int i = threadIdx.x; i < NT * W; i += kThreads) {
-        const int col = i % W;
-        float v = 0.f;
-        if (col < ncols) {
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) v += red_s[w * NT * W + i];
-        }
-        res[i] = v;
-    }
-    __syncthreads();
-    return res;
-}
-
-// Does expert e's factor have any INT8 group?  (prefix counts of the stacked tensor)
-__device__ __forceinline__ bool expert_has_int8(const latent_qmatrix &m, int e) {
-    if (!m.i8_mask) return false;
-    const int64_t words = ((m.rows * m.cols >> 5) + 31) >> 5;
-    const uint32_t *mask = m.i8_mask + (int64_t)e * words;
-    const uint32_t *base = m.i8_base + (int64_t)e * words;
-    const uint32_t first = __ldg(base), last = __ldg(base + words - 1) + __popc(__ldg(mask + words - 1));
-    return last > first;
-}
-
-// Adds the high-nibble part of every INT8 group of the tile to the CTA's
-// reduced sums res[t * W + col] (the main loop decoded only the low nibble,
-// through the identity table): value = (16*h + l) * |scale| with h the
-// signed high nibble from the i8_hi side table.  Per chunk of 256 rows it
-// makes two round trips to memory: (1) the mask and prefix words of every
-// row, (2) the high-nibble records and scale words of every INT8 group.
-// Deterministic: thread (column chunk of 8, row slice) accumulates its rows
-// in order, then the slices are summed in order.  `part` needs 8*NT*W
-// floats; `scratch` kI8Scratch bytes.
-constexpr int kI8Rows = 256;
-constexpr int kI8Cap = 512;
-constexpr int kI8Scratch = kI8Rows * 16 + kI8Rows * 8 + 64 + kI8Cap * 20;
-static_assert(kI8Rows == kThreads, "int8_fix scans one row per thread");
-
-template <int NT>
-__device__ void int8_fix(const QView &M, int row0, int row_end, int col0, int ncols, const float *in_s, int in_ld,
-                         float *res, int W, float *part, uint8_t *scratch) {
-    const int ng = ncols >> 5, g0 = col0 >> 5;
-    const int64_t gpr = M.cols >> 5;
-    const int64_t words = (((int64_t)M.rows * gpr) + 31) >> 5;
-    const int ccount = ncols >> 3;
-    const int slices = min(8, kThreads / ccount);
-    const int cc = threadIdx.x % ccount, sl = threadIdx.x / ccount;
-    const bool active = sl < slices;
-    const int col8 = cc * 8, gi = col8 >> 5, wsel = (col8 & 31) >> 3;
-    uint32_t *msk = reinterpret_cast<uint32_t *>(scratch);                    // [kI8Rows][2]
-    uint32_t *bas = msk + 2 * kI8Rows;                                         // [kI8Rows][2]
-    uint32_t *rowbits = bas + 2 * kI8Rows;                                     // [kI8Rows]
-    int *rowstart = reinterpret_cast<int *>(rowbits + kI8Rows);                // [kI8Rows + 1 + kWarps]
-    uint4 *ent_hi = reinterpret_cast<uint4 *>(scratch + kI8Rows * 16 + kI8Rows * 8 + 64);  // [kI8Cap]
-    float *ent_sc = reinterpret_cast<float *>(ent_hi + kI8Cap);               // [kI8Cap] 16*|scale|
-    float acc[NT][8];
-#pragma unroll
-    for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[t][j] = 0.f;
-    for (int rc = row0; rc < row_end;) {
-        int nr = min(kI8Rows, row_end - rc);
-        __syncthreads();
-        // round trip 1: mask and prefix words of each row's tile groups
-        for (int i = threadIdx.x; i < nr; i += kThreads) {
-            const int64_t pos = (int64_t)(rc + i) * gpr + g0;
-            const int64_t w = pos >> 5;
-            cp_async4(msk + 2 * i, M.i8.mask + w);
-            cp_async4(bas + 2 * i, M.i8.base + w);
-            if ((int)(pos & 31) + ng > 32 && w + 1 < words) {
-                cp_async4(msk + 2 * i + 1, M.i8.mask + w + 1);
-                cp_async4(bas + 2 * i + 1, M.i8.base + w + 1);
-            } else {
-                msk[2 * i + 1] = 0u;
-            }
-        }
-        cp_commit();
-        cp_wait<0>();
-        __syncthreads();
-        {   // one row per thread (kI8Rows == kThreads): bits, then a block scan of their counts
-            const int i = threadIdx.x, lane = i & 31, wid = i >> 5;
-            uint32_t bits = 0u;
-            if (i < nr) {
-                const int64_t pos = (int64_t)(rc + i) * gpr + g0;
-                const int b = (int)(pos & 31);
-                const uint64_t two = (uint64_t)msk[2 * i] | ((uint64_t)msk[2 * i + 1] << 32);
-                bits = (uint32_t)(two >> b) & ((1u << ng) - 1u);
-                rowbits[i] = bits;
-            }
-            const int c = __popc(bits);
-            int v = c;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, v, o);
-                if (lane >= o) v += y;
-            }
-            if (lane == 31) rowstart[kI8Rows + 1 + wid] = v;  // warp totals (scratch slots)
-            __syncthreads();
-            int base = 0;
-            for (int w2 = 0; w2 < wid; ++w2) base += rowstart[kI8Rows + 1 + w2];
-            const int start = base + v - c;
-            const bool ok = i < nr && start + c <= kI8Cap;
-            __syncthreads();
-            if (ok) rowstart[i] = start;
-            nr = __syncthreads_count(ok);  // rows handled this pass (a prefix of the chunk)
-        }
-        // round trip 2: high-nibble records and scale words of the INT8 groups
-        for (int i = threadIdx.x; i < nr; i += kThreads) {
-            const int64_t pos = (int64_t)(rc + i) * gpr + g0;
-            const int b = (int)(pos & 31);
-            int k = rowstart[i];
-            for (uint32_t rest = rowbits[i]; rest; rest &= rest - 1, ++k) {
-                const int q = __ffs(rest) - 1;
-                const int bb = b + q;                       // bit position relative to word w
-                const int wi = bb >> 5;                     // 0 or 1
-                const uint32_t mw = msk[2 * i + wi];
-                const uint32_t idx = bas[2 * i + wi] + __popc(mw & ((1u << (bb & 31)) - 1u));
-                cp_async16(ent_hi + k, M.i8.hi + (int64_t)idx * 16);
-                ent_sc[k] = 16.f * half_bits_to_float(__ldg(M.scales + pos + q) & 0x7FFFu);
-            }
-        }
-        cp_commit();
-        cp_wait<0>();
-        __syncthreads();
-        if (active) {
-            for (int rr = sl; rr < nr; rr += slices) {
-                const uint32_t bits = rowbits[rr];
-                if (!((bits >> gi) & 1u)) continue;
-                const int k = rowstart[rr] + __popc(bits & ((1u << gi) - 1u));
-                const uint32_t hw = reinterpret_cast<const uint32_t *>(ent_hi + k)[wsel];
-                const float s16 = ent_sc[k];
-                float xv[NT];
-#pragma unroll
-                for (int t = 0; t < NT; ++t) xv[t] = in_s[t * in_ld + (rc - row0 + rr)] * s16;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float h = (float)((int)(((hw >> (4 * j)) & 15u) ^ 8u) - 8);
-#pragma unroll
-                    for (int t = 0; t < NT; ++t) acc[t][j] = fmaf(xv[t], h, acc[t][j]);
-                }
-            }
-        }
-        rc += nr;
-    }
-    __syncthreads();
-    if (active) {
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) part[(sl * NT + t) * W + col8 + j] = acc[t][j];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int t = 0; t < NT; ++t)
-        for (int col = threadIdx.x; col < ncols; col += kThreads) {
-            float s = 0.f;
-            for (int q = 0; q < slices; ++q) s += part[(q * NT + t) * W + col];
-            res[t * W + col] += s;
-        }
-    __syncthreads();
-}
-
-struct Smem {
-    float *lut;    // 32: NF4 levels, then the identity table 0..15
-    uint8_t *stages;  // kStages * kStageBytes
-    uint8_t *i8s;     // kI8Scratch
-    float *in_s;   // staged input vectors
-    float *red_s;  // (kWarps+1) * 4 * max(r, kTileN)
-    float *g_s;    // 4 * kTileN
-    int *list;     // kThreads token ids
-    int *flag;     // 2 ints
+// ---------------------------------------------------------------------------
+// Phase geometry.  A phase has M matrices (1 or 2) of C column tiles of L
+// rows; segment j is (m = j / C, c = j % C), except in phase 2 where it is
+// (c = j / 2, m = j % 2) so that the gate and up tiles of a column range are
+// neighbours.  Work units: an 8-row block of a tile of width w weighs w / 32.
+struct Geo {
+    int P;        // 1..4
+    int M, C, L;  // matrices, tiles, rows
+    int N;        // matrix columns
+    int S;        // segments per virtual expert
+    int wl;       // width of the last tile
+    int Gp;       // warps the phase is spread over
+    int pstride;  // floats per partial-sum slot: kNT * min(256, N)
+    int pad;
+    int64_t Uf, Ul, Wm, Wv;  // units of a full tile, the last tile, a matrix, a virtual expert
+    int64_t total;           // units of the phase
 };
 
-__device__ __forceinline__ void cta_wait(const uint32_t *flag, uint32_t target, const DecodeArgs &a, const Smem &S) {
-    if (threadIdx.x == 0) wait_ge(flag, target, a.rt.err);
-    __syncthreads();
+__device__ __forceinline__ int tile_w(const Geo &g, int c) { return c == g.C - 1 ? g.wl : 256; }
+__device__ __forceinline__ int seg_m(const Geo &g, int j) { return g.P == 2 ? (j & 1) : j / g.C; }
+__device__ __forceinline__ int seg_c(const Geo &g, int j) { return g.P == 2 ? (j >> 1) : j % g.C; }
+__device__ __forceinline__ int64_t seg_off(const Geo &g, int j) {
+    const int m = seg_m(g, j), c = seg_c(g, j);
+    if (g.P == 2) return (int64_t)c * 2 * g.Uf + (int64_t)m * (c == g.C - 1 ? g.Ul : g.Uf);
+    return (int64_t)m * g.Wm + (int64_t)c * g.Uf;
 }
 
-// Publishes this CTA's global writes, then adds 1 to *ctr; returns the old value (all threads).
-__device__ __forceinline__ uint32_t cta_arrive(uint32_t *ctr, const Smem &S) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) S.flag[0] = (int)atomicAdd(ctr, 1u);
-    __syncthreads();
-    return (uint32_t)S.flag[0];
+__device__ Geo make_geo(const DecodeArgs &a, int P, int n_virt, int G) {
+    Geo g;
+    g.P = P;
+    g.L = P == 1 ? a.d : P == 2 ? a.r : P == 3 ? a.f : a.r;
+    g.N = P == 1 ? a.r : P == 2 ? a.f : P == 3 ? a.r : a.d;
+    g.M = P <= 2 ? 2 : 1;
+    g.C = (g.N + 255) / 256;
+    g.S = g.M * g.C;
+    g.wl = g.N - 256 * (g.C - 1);
+    g.Uf = (int64_t)(g.L / 8) * 8;
+    g.Ul = (int64_t)(g.L / 8) * (g.wl / 32);
+    g.Wm = (int64_t)(g.C - 1) * g.Uf + g.Ul;
+    g.Wv = g.Wm * g.M;
+    g.total = g.Wv * n_virt;
+    const int64_t gp = (g.total + kMinUnits - 1) / kMinUnits;
+    g.Gp = (int)(gp < G ? gp : G);
+    if (g.Gp < 1) g.Gp = 1;
+    g.pstride = kNT * (g.N < 256 ? g.N : 256);
+    g.pad = 0;
+    return g;
 }
 
-template <int LPR, int NT>
-__device__ __forceinline__ void in_chunk(const QView &M, bool has_i8, int row0, int row_end, int r, const float *in_s,
-                                         int kc, const Smem &S, float *part_rows, int ldo, bool pre) {
-    u64 acc[NT][8];
-    if (pre)
-        vecmat_staged<LPR, NT, kLoop>(M, row0, row_end, 0, r, in_s, kc, S.lut, S.stages, acc);
-    else
-        vecmat_staged<LPR, NT>(M, row0, row_end, 0, r, in_s, kc, S.lut, S.stages, acc);
-    float *res = cta_reduce<LPR, NT>(acc, r, S.red_s);
-    if (has_i8) int8_fix<NT>(M, row0, row_end, 0, r, in_s, kc, res, LPR * 16, S.red_s, S.i8s);
-#pragma unroll
-    for (int t = 0; t < NT; ++t)
-        for (int col = threadIdx.x; col < r; col += kThreads) part_rows[(int64_t)t * ldo + col] = res[t * r + col];
+struct Pos {
+    int v, j, blk;
+};
+
+// The block containing unit u (0 <= u < total).
+__device__ Pos pos_of(const Geo &g, int64_t u) {
+    Pos p;
+    p.v = (int)(u / g.Wv);
+    const int64_t rem = u - (int64_t)p.v * g.Wv;
+    int c;
+    int64_t r3;
+    if (g.P == 2) {
+        c = (int)(rem / (2 * g.Uf));
+        if (c > g.C - 1) c = g.C - 1;
+        const int64_t r2 = rem - (int64_t)c * 2 * g.Uf;
+        const int64_t U = c == g.C - 1 ? g.Ul : g.Uf;
+        const int m = (int)(r2 / U);
+        r3 = r2 - m * U;
+        p.j = 2 * c + m;
+    } else {
+        const int m = (int)(rem / g.Wm);
+        const int64_t r2 = rem - (int64_t)m * g.Wm;
+        c = (int)(r2 / g.Uf);
+        if (c > g.C - 1) c = g.C - 1;
+        r3 = r2 - (int64_t)c * g.Uf;
+        p.j = m * g.C + c;
+    }
+    p.blk = (int)(r3 / (tile_w(g, c) / 32));
+    return p;
 }
 
-// Phase 1 (PH=1: t = x.A_{g|u}) and phase 3 (PH=3: s = h.A_d): one split-K row chunk.
-template <int LPR, int XT, int PH>
-__device__ void item_in(const DecodeArgs &a, const Smem &S, int ai, int m, int ksel) {
-    constexpr int nmat = PH == 1 ? 2 : 1;
-    const int kc = PH == 1 ? a.kc1 : a.kc2, ks = PH == 1 ? a.ks1 : a.ks2, r = a.r;
-    const int e = a.rt.active[ai];
-    const int p0 = a.rt.offsets[e], ne = a.rt.offsets[e + 1] - p0;
-    const latent_qmatrix &qm = PH == 1 ? (m == 0 ? a.gate_a : a.up_a) : a.down_a;
-    const QView M = expert_view(qm, e);
-    const bool has_i8 = expert_has_int8(qm, e);
-    const int row0 = ksel * kc, row_end = min(M.rows, row0 + kc);
-    {   // start streaming the weights before waiting for inputs
-        u64 none[1][8];
-        vecmat_staged<LPR, 1, kPrologue>(M, row0, row_end, 0, r, nullptr, 0, S.lut, S.stages, none);
-    }
-    if (PH == 3) cta_wait(a.cnt2 + e, (uint32_t)a.nct_f, a, S);
-    const int ldo = nmat * r;
-    float *part = PH == 1 ? a.part1 : a.part2;
-    for (int tc = 0; tc < ne; tc += 4) {
-        const int nt = min(4, ne - tc);
-        __syncthreads();
-        for (int t = 0; t < nt; ++t) {
-            const int p = p0 + tc + t;
-            const int64_t src = PH == 1 ? (int64_t)(a.rt.order[p] / a.k) * a.d : (int64_t)p * a.f;
-            for (int rr = threadIdx.x; rr < kc; rr += kThreads) {
-                const int row = row0 + rr;
-                float v = 0.f;
-                if (row < row_end) {
-                    if constexpr (PH == 1)
-                        v = load_act<XT>(a.x, src + row);
-                    else
-                        v = __ldcg(a.h + src + row);
-                }
-                S.in_s[t * kc + rr] = v;
-            }
-        }
-        __syncthreads();
-        float *rows = part + ((int64_t)ksel * a.R + p0 + tc) * ldo + m * r;
-        if (nt == 1)
-            in_chunk<LPR, 1>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo, tc == 0);
-        else if (nt == 2)
-            in_chunk<LPR, 2>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo, tc == 0);
-        else if (nt == 3)
-            in_chunk<LPR, 3>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo, tc == 0);
-        else
-            in_chunk<LPR, 4>(M, has_i8, row0, row_end, r, S.in_s, kc, S, rows, ldo, tc == 0);
-    }
-    uint32_t *arr = (PH == 1 ? a.arr1 : a.arr3) + e;
-    if (cta_arrive(arr, S) != (uint32_t)(nmat * ks - 1)) return;
-    // Last chunk of this expert: sum the partials in chunk order, publish.
-    __threadfence();
-    float *outv = PH == 1 ? a.t : a.s;
-    for (int pp = p0; pp < p0 + ne; ++pp) {
-        for (int col = threadIdx.x; col < ldo; col += kThreads) {
-            float v = 0.f;
-            for (int q = 0; q < ks; ++q) v += __ldcg(part + ((int64_t)q * a.R + pp) * ldo + col);
-            outv[(int64_t)pp * ldo + col] = v;
-        }
-    }
-    cta_arrive(PH == 1 ? a.flag1 + e : a.flag3 + e, S);
+// First block of warp w's range (w in [0, Gp]); warp w owns [start(w), start(w+1)).
+__device__ Pos range_start(const Geo &g, int w, int n_virt) {
+    const int64_t u = g.total * w / g.Gp;
+    if (u >= g.total) return Pos{n_virt, 0, 0};
+    return pos_of(g, u);
 }
 
-template <int NT>
-__device__ __forceinline__ void gateup_chunk(const DecodeArgs &a, const Smem &S, const QView &Mg, bool gi8,
-                                             const QView &Mu, bool ui8, int col0, int ncols, int p,
-                                             const float *in_g, const float *in_u, bool pre) {
-    constexpr int W = kTileN;
-    const int r = a.r;
-    u64 acc[NT][8];
-    if (pre)
-        vecmat_staged<16, NT, kLoop>(Mg, 0, r, col0, ncols, in_g, r, S.lut, S.stages, acc);
-    else
-        vecmat_staged<16, NT>(Mg, 0, r, col0, ncols, in_g, r, S.lut, S.stages, acc);
-    {   // the up matrix starts streaming while the gate sums are reduced
-        u64 none[1][8];
-        vecmat_staged<16, 1, kPrologue>(Mu, 0, r, col0, ncols, nullptr, 0, S.lut, S.stages, none);
-    }
-    float *res = cta_reduce<16, NT>(acc, ncols, S.red_s);
-    if (gi8) int8_fix<NT>(Mg, 0, r, col0, ncols, in_g, r, res, W, S.red_s, S.i8s);
-    for (int i = threadIdx.x; i < NT * W; i += kThreads) S.g_s[i] = res[i];
-    __syncthreads();
-    vecmat_staged<16, NT, kLoop>(Mu, 0, r, col0, ncols, in_u, r, S.lut, S.stages, acc);
-    res = cta_reduce<16, NT>(acc, ncols, S.red_s);
-    if (ui8) int8_fix<NT>(Mu, 0, r, col0, ncols, in_u, r, res, W, S.red_s, S.i8s);
-    const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
-    for (int i = threadIdx.x; i < NT * W; i += kThreads) {
-        const int t = i / W, col = i - t * W;
-        if (col >= ncols) continue;
-        float hv = silu_f32(S.g_s[i]) * res[i];
-        if (wbd) hv *= load_weight(a.weights, a.w_type, a.rt.order[p + t]);
-        a.h[(int64_t)(p + t) * a.f + col0 + col] = hv;
-    }
+__device__ __forceinline__ bool pos_less(const Pos &a, const Pos &b) {
+    return a.v != b.v ? a.v < b.v : a.j != b.j ? a.j < b.j : a.blk < b.blk;
 }
 
-// Phase 2: h = silu(t_g.B_g) * (t_u.B_u) [* w] for one 256-column tile of f.
-__device__ void item_gateup(const DecodeArgs &a, const Smem &S, int ai, int ct) {
-    const int r = a.r;
-    const int e = a.rt.active[ai];
-    const int p0 = a.rt.offsets[e], ne = a.rt.offsets[e + 1] - p0;
-    const QView Mg = expert_view(a.gate_b, e), Mu = expert_view(a.up_b, e);
-    const bool gi8 = expert_has_int8(a.gate_b, e), ui8 = expert_has_int8(a.up_b, e);
-    const int col0 = ct * kTileN, ncols = min(kTileN, a.f - col0);
-    {
-        u64 none[1][8];
-        vecmat_staged<16, 1, kPrologue>(Mg, 0, r, col0, ncols, nullptr, 0, S.lut, S.stages, none);
-    }
-    cta_wait(a.flag1 + e, 1u, a, S);
-    float *in_g = S.in_s, *in_u = S.in_s + 4 * r;
-    for (int tc = 0; tc < ne; tc += 4) {
-        const int nt = min(4, ne - tc);
-        __syncthreads();
-        for (int t = 0; t < nt; ++t) {
-            const float *src = a.t + (int64_t)(p0 + tc + t) * 2 * r;
-            for (int kk = threadIdx.x; kk < r; kk += kThreads) {
-                in_g[t * r + kk] = __ldcg(src + kk);
-                in_u[t * r + kk] = __ldcg(src + r + kk);
-            }
-        }
-        __syncthreads();
-        const int p = p0 + tc;
-        if (nt == 1)
-            gateup_chunk<1>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u, tc == 0);
-        else if (nt == 2)
-            gateup_chunk<2>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u, tc == 0);
-        else if (nt == 3)
-            gateup_chunk<3>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u, tc == 0);
-        else
-            gateup_chunk<4>(a, S, Mg, gi8, Mu, ui8, col0, ncols, p, in_g, in_u, tc == 0);
-    }
-    cta_arrive(a.cnt2 + e, S);
+// The warp owning block blk of segment (v, j): the last w with start(w) <= block.
+__device__ int owner(const Geo &g, int v, int j, int blk) {
+    const int wb = tile_w(g, seg_c(g, j)) / 32;
+    const int64_t end = (int64_t)v * g.Wv + seg_off(g, j) + (int64_t)(blk + 1) * wb;
+    int w = (int)((end * g.Gp + g.total - 1) / g.total) - 1;
+    if (w < 0) w = 0;
+    if (w > g.Gp - 1) w = g.Gp - 1;
+    return w;
 }
 
-template <int NT>
-__device__ __forceinline__ void down_chunk(const DecodeArgs &a, const Smem &S, const QView &M, bool i8, int col0,
-                                           int ncols, int p, bool pre) {
-    constexpr int W = kTileN;
-    u64 acc[NT][8];
-    if (pre)
-        vecmat_staged<16, NT, kLoop>(M, 0, a.r, col0, ncols, S.in_s, a.r, S.lut, S.stages, acc);
-    else
-        vecmat_staged<16, NT>(M, 0, a.r, col0, ncols, S.in_s, a.r, S.lut, S.stages, acc);
-    float *res = cta_reduce<16, NT>(acc, ncols, S.red_s);
-    if (i8) int8_fix<NT>(M, 0, a.r, col0, ncols, S.in_s, a.r, res, W, S.red_s, S.i8s);
-    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
-    for (int i = threadIdx.x; i < NT * W; i += kThreads) {
-        const int t = i / W, col = i - t * W;
-        if (col >= ncols) continue;
-        if (per_slot)
-            a.out[(int64_t)a.rt.order[p + t] * a.d + col0 + col] = res[i];
-        else
-            a.y[(int64_t)(p + t) * a.d + col0 + col] = res[i];
-    }
-}
+// ---------------------------------------------------------------------------
+// Piece iteration: the pieces of a warp's ranges in phase order.  The
+// consumer and the stage issuer each run one iterator over the same sequence
+// (kept in the warp's shared area between pieces).
+struct Iter {
+    int P;         // phase of the current piece (5 once all ranges are done)
+    Pos cur, end;  // start of the next piece, end of the warp's range in phase P
+    int v, j;      // current piece: virtual expert, segment
+    int row, row1; // first row, end row of the piece
+};
+static_assert(sizeof(Iter) <= 48, "iterator area");
 
-__device__ __forceinline__ int live_slots(const DecodeArgs &a, int t) {
-    int n = 0;
-    for (int j = 0; j < a.k; ++j) n += a.rt.pos[t * a.k + j] >= 0;
-    return n;
-}
-
-// Phase 4: y = s.B_d for one 256-column tile of d, then the top-k combine of
-// every token whose last routed slot for this tile just finished.
-__device__ void item_down(const DecodeArgs &a, const Smem &S, int ai, int ct) {
-    const int r = a.r;
-    const int e = a.rt.active[ai];
-    const int p0 = a.rt.offsets[e], ne = a.rt.offsets[e + 1] - p0;
-    const QView M = expert_view(a.down_b, e);
-    const bool i8 = expert_has_int8(a.down_b, e);
-    const int col0 = ct * kTileN, ncols = min(kTileN, a.d - col0);
-    {
-        u64 none[1][8];
-        vecmat_staged<16, 1, kPrologue>(M, 0, r, col0, ncols, nullptr, 0, S.lut, S.stages, none);
-    }
-    cta_wait(a.flag3 + e, 1u, a, S);
-    for (int tc = 0; tc < ne; tc += 4) {
-        const int nt = min(4, ne - tc);
-        __syncthreads();
-        for (int t = 0; t < nt; ++t)
-            for (int kk = threadIdx.x; kk < r; kk += kThreads)
-                S.in_s[t * r + kk] = __ldcg(a.s + (int64_t)(p0 + tc + t) * r + kk);
-        __syncthreads();
-        const int p = p0 + tc;
-        if (nt == 1)
-            down_chunk<1>(a, S, M, i8, col0, ncols, p, tc == 0);
-        else if (nt == 2)
-            down_chunk<2>(a, S, M, i8, col0, ncols, p, tc == 0);
-        else if (nt == 3)
-            down_chunk<3>(a, S, M, i8, col0, ncols, p, tc == 0);
-        else
-            down_chunk<4>(a, S, M, i8, col0, ncols, p, tc == 0);
-    }
-    if (a.flags & LATENT_FLAG_OUT_PER_SLOT) return;
-    __threadfence();
-    const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
-    for (int base = 0; base < ne; base += kThreads) {
-        __syncthreads();
-        if (threadIdx.x == 0) S.flag[1] = 0;
-        __syncthreads();
-        const int i = base + threadIdx.x;
-        if (i < ne) {
-            const int t = a.rt.order[p0 + i] / a.k;
-            const uint32_t old = atomicAdd(a.tokcnt + (int64_t)t * a.nct_d + ct, 1u);
-            if ((int)old + 1 == live_slots(a, t)) S.list[atomicAdd(&S.flag[1], 1)] = t;
-        }
-        __syncthreads();
-        const int n_done = S.flag[1];
-        if (n_done == 0) continue;
-        __threadfence();
-        for (int q = 0; q < n_done; ++q) {
-            const int t = S.list[q];
-            for (int col = threadIdx.x; col < ncols; col += kThreads) {
-                float acc = 0.f;
-                for (int j = 0; j < a.k; ++j) {
-                    const int slot = t * a.k + j;
-                    const int pp = a.rt.pos[slot];
-                    if (pp < 0) continue;
-                    const float w = wbd ? 1.f : load_weight(a.weights, a.w_type, slot);
-                    acc = fmaf(w, __ldcg(a.y + (int64_t)pp * a.d + col0 + col), acc);
-                }
-                a.out[(int64_t)t * a.d + col0 + col] = acc;
-            }
-        }
-    }
-}
-
-template <int LPR, int XT>
-__global__ void __launch_bounds__(kThreads, 2) k_decode(DecodeArgs a) {
-    extern __shared__ __align__(128) uint8_t sm_raw[];
-    __shared__ __align__(128) float s_lut[32];
-    __shared__ int s_list[kThreads];
-    __shared__ int s_flag[2];
-    __shared__ int s_item;
-    Smem S;
-    S.lut = s_lut;
-    S.stages = sm_raw;
-    S.i8s = sm_raw + kStages * kStageBytes;
-    float *sm = reinterpret_cast<float *>(sm_raw + kStages * kStageBytes + kI8Scratch);
-    S.in_s = sm;
-    S.red_s = sm + a.in_floats;
-    S.g_s = S.red_s + a.red_floats;
-    S.list = s_list;
-    S.flag = s_flag;
-    if (threadIdx.x < 16) s_lut[threadIdx.x] = kNF4Levels[threadIdx.x];
-    else if (threadIdx.x < 32) s_lut[threadIdx.x] = (float)(threadIdx.x - 16);
-    const int n_active = *a.rt.n_active;
-    const int n1 = n_active * 2 * a.ks1, n2 = n_active * a.nct_f, n3 = n_active * a.ks2, n4 = n_active * a.nct_d;
-    // Rows no expert writes: skipped slots (per-slot output) or tokens with no live slot.
-    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
-    const int n_rows = per_slot ? a.T * a.k : a.T;
-    for (int i = blockIdx.x; i < n_rows; i += gridDim.x) {
-        const bool empty = per_slot ? a.rt.pos[i] < 0 : live_slots(a, i) == 0;
-        if (empty)
-            for (int c = threadIdx.x * 4; c < a.d; c += kThreads * 4)
-                *reinterpret_cast<float4 *>(a.out + (int64_t)i * a.d + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+// Moves to the next non-empty piece; false when all phases are done.
+__device__ bool iter_next(Iter &it, const Geo *geo, int gw, int n_virt) {
     while (true) {
-        __syncthreads();
-        if (threadIdx.x == 0) s_item = (int)atomicAdd(a.work, 1u);
-        __syncthreads();
-        int it = s_item;
-        if (it < n1) {
-            item_in<LPR, XT, 1>(a, S, it / (2 * a.ks1), (it / a.ks1) % 2, it % a.ks1);
+        if (it.P >= 1 && it.P <= 4 && pos_less(it.cur, it.end)) {
+            const Geo &g = geo[it.P - 1];
+            it.v = it.cur.v;
+            it.j = it.cur.j;
+            it.row = it.cur.blk * 8;
+            it.row1 = (it.cur.v == it.end.v && it.cur.j == it.end.j) ? it.end.blk * 8 : g.L;
+            if (++it.cur.j == g.S) {
+                it.cur.j = 0;
+                ++it.cur.v;
+            }
+            it.cur.blk = 0;
+            if (it.row1 > it.row) return true;
             continue;
         }
-        it -= n1;
-        if (it < n2) {
-            item_gateup(a, S, it / a.nct_f, it % a.nct_f);
-            continue;
+        if (it.P >= 4) {
+            it.P = 5;
+            return false;
         }
-        it -= n2;
-        if (it < n3) {
-            item_in<LPR, LATENT_TYPE_F32, 3>(a, S, it / a.ks2, 0, it % a.ks2);
-            continue;
+        ++it.P;
+        const Geo &g = geo[it.P - 1];
+        if (gw < g.Gp) {
+            it.cur = range_start(g, gw, n_virt);
+            it.end = range_start(g, gw + 1, n_virt);
+        } else {
+            it.cur = it.end = Pos{0, 0, 0};
         }
-        it -= n3;
-        if (it < n4) {
-            item_down(a, S, it / a.nct_d, it % a.nct_d);
-            continue;
-        }
-        break;
     }
 }
 
-int round_up(int x, int m) { return (x + m - 1) / m * m; }
-
-// Rows per split-K item: about 32 KB of codes, whole warp steps, at most 1024.
-void plan_split(int K, int r, int &kc, int &ks) {
-    const int lpr = r / 16;
-    const int step = kWarps * (32 / lpr);
-    int rows = 32768 / (r / 2);
-    rows = rows < step ? step : rows;
-    rows = rows > 512 ? 512 : rows;
-    kc = round_up(rows, 64);
-    if (kc > round_up(K, 64)) kc = round_up(K, 64);
-    ks = (K + kc - 1) / kc;
+__device__ __forceinline__ const latent_qmatrix &phase_matrix(const DecodeArgs &a, int P, int m) {
+    return P == 1 ? (m ? a.up_a : a.gate_a) : P == 2 ? (m ? a.up_b : a.gate_b) : P == 3 ? a.down_a : a.down_b;
 }
 
-template <int LPR>
-const void *decode_fn(int x_type) {
-    switch (x_type) {
-        case LATENT_TYPE_F32: return (const void *)k_decode<LPR, LATENT_TYPE_F32>;
-        case LATENT_TYPE_F16: return (const void *)k_decode<LPR, LATENT_TYPE_F16>;
-        default: return (const void *)k_decode<LPR, LATENT_TYPE_BF16>;
+// Iterator step shared by all lanes: load from the warp area, advance, store back.
+__device__ __forceinline__ bool shared_iter_next(Iter *itp, Iter &it, const Geo *geo, int gw, int n_virt, int lane) {
+    it = *itp;
+    const bool more = iter_next(it, geo, gw, n_virt);
+    __syncwarp();
+    if (lane == 0) *itp = it;
+    __syncwarp();
+    return more;
+}
+
+// Stage issuer: source pointers of the next stage of its current piece.
+struct Issuer {
+    const uint8_t *codes;
+    const uint8_t *scales;
+    int row, row1;  // next row, end row of the piece
+    int cstride;    // code bytes per row (tile width / 2)
+    int P;          // 0 before the first piece, 5 when all are issued
+    int pc;         // pieces entered
+};
+
+// Mask/base words of the INT8 table around expert-local group q: word
+// index, and whether q is past the last group (then all bits count).
+__device__ __forceinline__ int64_t int8_word(const latent_qmatrix &m, int64_t q, bool &past) {
+    const int64_t groups = m.rows * m.cols / 32, words = (groups + 31) / 32;
+    past = q >= groups;
+    return past ? words - 1 : (q >> 5);
+}
+
+// INT8 records before group q from the copied (base, mask) words.
+__device__ __forceinline__ uint32_t int8_count(uint32_t base, uint32_t mask, int64_t q, bool past) {
+    return base + __popc(past ? mask : (mask & ((1u << (q & 31)) - 1u)));
+}
+
+__device__ void issuer_next_piece(const DecodeArgs &a, Issuer &is, uint8_t *warea, const Geo *geo, int gw,
+                                  int n_virt, int lane) {
+    Iter it;
+    if (!shared_iter_next(reinterpret_cast<Iter *>(warea + kWIssue), it, geo, gw, n_virt, lane)) {
+        is.P = 5;
+        return;
+    }
+    const Geo &g = geo[it.P - 1];
+    const int m = seg_m(g, it.j), c = seg_c(g, it.j), w = tile_w(g, c), ng = w >> 5;
+    const int e = __ldg(&a.rt.virt[it.v].x);
+    const latent_qmatrix &qm = phase_matrix(a, it.P, m);
+    const int64_t q0 = (int64_t)c * g.L * 8 + (int64_t)it.row * ng;  // expert-local flat group
+    is.codes = qm.codes + (int64_t)e * (qm.rows * qm.cols / 2) + q0 * 16;
+    is.scales = reinterpret_cast<const uint8_t *>(qm.scales + (int64_t)e * (qm.rows * qm.cols / 32) + q0);
+    is.row = it.row;
+    is.row1 = it.row1;
+    is.cstride = w >> 1;
+    is.P = it.P;
+    // INT8 table words at the piece's first and end row; they land with the
+    // piece's first stage, before the consumer needs them.
+    if (qm.i8_mask && lane < 4) {
+        const int64_t words = (qm.rows * qm.cols / 32 + 31) / 32;
+        bool past;
+        const int64_t q = (int64_t)c * g.L * 8 + (int64_t)(lane < 2 ? it.row : it.row1) * ng;
+        const int64_t wi = (int64_t)e * words + int8_word(qm, q, past);
+        const uint32_t *src = (lane & 1) ? qm.i8_mask + wi : qm.i8_base + wi;
+        const uint32_t dst = smem_u32(warea + kWMeta + (is.pc & 3) * 16 + lane * 4);
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+    }
+    ++is.pc;
+}
+
+// Issues the next stage into ring slot `slot` (all lanes) and commits one
+// cp.async group (empty once everything is issued).
+__device__ __forceinline__ void issue_stage(const DecodeArgs &a, Issuer &is, uint8_t *warea, const Geo *geo, int gw,
+                                            int n_virt, uint32_t slot, int lane) {
+    if (is.P <= 4 && is.row >= is.row1) issuer_next_piece(a, is, warea, geo, gw, n_virt, lane);
+    if (is.P <= 4) {
+        const int n = min(kStRows, is.row1 - is.row);
+        const int cb = n * is.cstride;  // code bytes, a multiple of 128
+        for (int o = lane * 16; o < cb; o += 512) cp_async16(slot + o, is.codes + o);
+        const int sbytes = cb >> 3;     // scale bytes, a multiple of 16
+        if (lane * 16 < sbytes) cp_async16(slot + kStCode + lane * 16, is.scales + lane * 16);
+        is.codes += cb;
+        is.scales += sbytes;
+        is.row += n;
+    }
+    cp_commit();
+}
+
+// ---------------------------------------------------------------------------
+template <int NT>
+struct Mode {
+    static constexpr int COLS = NT <= 4 ? 16 : 8;  // columns per lane
+    static constexpr int NB = COLS / 2;            // code bytes per lane and row
+};
+
+// Inner loop over the n rows of one stage.  acc[t * NB + b] holds columns
+// (2b, 2b+1) of the lane's COLS columns for token t.
+template <int NT>
+__device__ __forceinline__ void stage_rows(uint32_t slot, int n, int w, int ng, int rs, int ch, int rps,
+                                           uint32_t in_s, uint32_t lb, u64 (&acc)[32]) {
+    constexpr int NB = Mode<NT>::NB, COLS = Mode<NT>::COLS;
+    const int wb = w >> 1;
+    const int gofs = (ch * COLS) >> 5;
+#pragma unroll 1
+    for (int row = rs; row < n; row += rps) {
+        const uint32_t cb = slot + row * wb + ch * NB;
+        uint32_t q[2];
+        if constexpr (NB == 8) {
+            const uint2 v = lds_v2(cb);
+            q[0] = v.x;
+            q[1] = v.y;
+        } else {
+            q[0] = lds32(cb);
+            q[1] = 0;
+        }
+        const uint32_t sb = lds16(slot + kStCode + (row * ng + gofs) * 2);
+        const uint32_t lr = lb | ((sb >> 8) & 0x80u);
+        const float sc = half_bits_to_float((uint16_t)(sb & 0x7FFFu));
+        const uint32_t xa = in_s + (uint32_t)row * (kNT * 4);
+        float xv[8];
+        {
+            const float4 x0 = lds_f4(xa);
+            xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
+            if constexpr (NT > 4) {
+                const float4 x1 = lds_f4(xa + 16);
+                xv[4] = x1.x; xv[5] = x1.y; xv[6] = x1.z; xv[7] = x1.w;
+            }
+        }
+        u64 xs[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const float v = xv[t] * sc;
+            xs[t] = pack2(v, v);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const uint32_t addr = __byte_perm(q[b >> 2], lr, 0x7604u | ((uint32_t)(b & 3) << 4));
+            const u64 vv = lds64(addr);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) ffma2(acc[t * NB + b], xs[t], vv);
+        }
     }
 }
 
-const void *pick_decode_fn(int r, int x_type) {
-    switch (r) {
-        case 32: return decode_fn<2>(x_type);
-        case 64: return decode_fn<4>(x_type);
-        case 128: return decode_fn<8>(x_type);
-        case 256: return decode_fn<16>(x_type);
-        case 512: return decode_fn<32>(x_type);
-        default: return nullptr;
+// INT8 flags of one stage (from its scales, still in the ring): lanes
+// 0..n-1 take row `lane`, store the row's record prefix and flags and the
+// scales of its INT8 groups (buffer `par`), and every lane gets the row mask
+// of its own group g.  Returns the stage's INT8 record count.
+__device__ __forceinline__ int stage_flags(uint32_t slot, int n, int ng, int g, int lane, uint8_t *warea, int par,
+                                           uint32_t &mask) {
+    uint32_t flags = 0;
+    if (lane < n) {
+        uint16_t *stash = reinterpret_cast<uint16_t *>(warea + kWStash + par * (kStRows * 16) + lane * 16);
+        for (int gg = 0; gg < ng; ++gg) {
+            const uint32_t sb = lds16(slot + kStCode + (lane * ng + gg) * 2);
+            if (sb & 0x8000u) {
+                flags |= 1u << gg;
+                stash[gg] = (uint16_t)sb;
+            }
+        }
     }
+    const int cnt = __popc(flags);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if ((lane & 15) >= o) incl += y;
+    }
+    if (lane < n)
+        *reinterpret_cast<uint16_t *>(warea + kWRow + par * (kStRows * 2) + lane * 2) =
+            (uint16_t)((incl - cnt) | (flags << 8));
+    mask = 0;
+    for (int gg = 0; gg < ng; ++gg) {
+        const uint32_t b = __ballot_sync(0xffffffffu, (flags >> gg) & 1u);
+        if (gg == g) mask = b & 0xFFFFu;
+    }
+    return __shfl_sync(0xffffffffu, incl, 15);
+}
+
+// INT8 high-nibble pass of a stage whose flags, scales, inputs and records
+// sit in the buffers of parity `par`: the lane adds 16 * (hi' - 8) + 8 for
+// its share of the rows of its own group (records past the first kRecStage
+// are read from global memory at hi_stage).
+template <int NT>
+__device__ __forceinline__ void int8_pass(uint32_t wbase, int par, uint32_t mask, int g, int rs, int ch, int rps,
+                                          const uint8_t *hi_stage, uint32_t lb, u64 (&acc)[32]) {
+    constexpr int NB = Mode<NT>::NB, COLS = Mode<NT>::COLS;
+    const int colb = ((ch * COLS) & 31) >> 1;  // byte offset of the lane's nibbles in a record
+    const int cntg = __popc(mask);
+    const int beg = rs * cntg / rps, end = (rs + 1) * cntg / rps;
+    if (beg >= end) return;
+    int row = (int)__fns(mask, 0, beg + 1);
+    const uint32_t lr = lb | 0x80u;
+    const uint32_t rowb = wbase + kWRow + par * (kStRows * 2);
+    const uint32_t stb = wbase + kWStash + par * (kStRows * 16);
+    const uint32_t recb = wbase + kWRec + par * (kRecStage * 16);
+    const uint32_t inb = wbase + kWIn + par * (kStRows * kNT * 4);
+    float cc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) cc[t] = 0.f;
+    for (int it = beg; it < end; ++it) {
+        const uint32_t ri = lds16(rowb + row * 2);
+        const int idx = (int)(ri & 0xFFu) + __popc((ri >> 8) & ((1u << g) - 1u));
+        uint32_t hw[2];
+        if (idx < kRecStage) {
+            const uint32_t ra = recb + idx * 16 + colb;
+            if constexpr (NB == 8) {
+                const uint2 v = lds_v2(ra);
+                hw[0] = v.x;
+                hw[1] = v.y;
+            } else {
+                hw[0] = lds32(ra);
+                hw[1] = 0;
+            }
+        } else {
+            const uint8_t *p = hi_stage + (int64_t)idx * 16 + colb;
+            if constexpr (NB == 8) {
+                const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p));
+                hw[0] = v.x;
+                hw[1] = v.y;
+            } else {
+                hw[0] = __ldg(reinterpret_cast<const uint32_t *>(p));
+                hw[1] = 0;
+            }
+        }
+        hw[0] ^= 0x88888888u;
+        hw[1] ^= 0x88888888u;
+        const uint32_t sb = lds16(stb + row * 16 + g * 2);
+        const float sc = half_bits_to_float((uint16_t)(sb & 0x7FFFu));
+        const uint32_t xa = inb + (uint32_t)row * (kNT * 4);
+        float xv[8];
+        {
+            const float4 x0 = lds_f4(xa);
+            xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
+            if constexpr (NT > 4) {
+                const float4 x1 = lds_f4(xa + 16);
+                xv[4] = x1.x; xv[5] = x1.y; xv[6] = x1.z; xv[7] = x1.w;
+            }
+        }
+        u64 xs[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const float v = xv[t] * sc;
+            cc[t] = fmaf(8.f, v, cc[t]);
+            const float v16 = 16.f * v;
+            xs[t] = pack2(v16, v16);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const uint32_t addr = __byte_perm(hw[b >> 2], lr, 0x7604u | ((uint32_t)(b & 3) << 4));
+            const u64 vv = lds64(addr);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) ffma2(acc[t * NB + b], xs[t], vv);
+        }
+        const uint32_t rest = row >= 31 ? 0u : mask & (0xFFFFFFFEu << row);
+        row = __ffs(rest) - 1;
+    }
+    // the "+ 8" of every INT8 group visited, on all of the lane's columns
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const u64 k = pack2(cc[t], cc[t]);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) acc[t * NB + b] = fadd2(acc[t * NB + b], k);
+    }
+}
+
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float load_x(const DecodeArgs &a, int64_t i) {
+    switch (a.x_type) {
+        case LATENT_TYPE_F32: return __ldg(reinterpret_cast<const float *>(a.x) + i);
+        case LATENT_TYPE_F16: return __half2float(__ldg(reinterpret_cast<const __half *>(a.x) + i));
+        default: return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16 *>(a.x) + i));
+    }
+}
+
+// Inputs of one stage row for tokens 4*tq .. 4*tq+3 (zero when not live).
+__device__ __forceinline__ void load_inputs(const DecodeArgs &a, int P, int m, int p0, int nt, int row, bool live,
+                                            int tq, const int *tok, float (&pre)[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int t = 4 * tq + k;
+        float v = 0.f;
+        if (live && t < nt) {
+            const int p = p0 + t;
+            if (P == 1)
+                v = load_x(a, (int64_t)tok[t] * a.d + row);
+            else if (P == 2)
+                v = __ldcg(a.t + (int64_t)p * 2 * a.r + m * a.r + row);
+            else if (P == 3)
+                v = __ldcg(a.h + (int64_t)p * a.f + row);
+            else
+                v = __ldcg(a.s + (int64_t)p * a.r + row);
+        }
+        pre[k] = v;
+    }
+}
+
+// Index of the arrival counter / ready flag of segment (v, j) of phase P.
+__device__ __forceinline__ int flag_index(const Geo &g, int v, int j) {
+    return g.P == 2 ? v * g.C + (j >> 1) : v * g.S + j;
+}
+
+// The piece that completes segment (v, j) (phase 2: the gate/up pair of
+// tile c) sums the partials in piece order and writes the phase output.
+__device__ __noinline__ void finalize(const DecodeArgs &a, const Geo &g, int v, int j, int lane) {
+    const int4 ve = __ldg(&a.rt.virt[v]);
+    const int p0 = ve.y, nt = ve.z;
+    const int c = seg_c(g, j), w = tile_w(g, c), w4 = w >> 2;
+    const int tw = g.pstride / kNT;
+    const float *part = a.part[g.P - 1];
+    const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
+    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
+    const int j0 = g.P == 2 ? (j & ~1) : j, nj = g.P == 2 ? 2 : 1;
+    const int n4 = nt * w4;
+    for (int i0 = lane; i0 < n4; i0 += 128) {
+        float4 sum[2][4];
+        for (int q = 0; q < nj; ++q) {
+            const int64_t sg = (int64_t)v * g.S + j0 + q;
+            const int first = owner(g, v, j0 + q, 0), last = owner(g, v, j0 + q, g.L / 8 - 1);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sum[q][e] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int pw = first; pw <= last; pw += 4) {
+                float4 x[4][4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int i = i0 + 32 * e;
+                        x[k][e] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (i < n4 && pw + k <= last) {
+                            const int t = i / w4, c4 = (i - t * w4) * 4;
+                            x[k][e] = __ldcg(reinterpret_cast<const float4 *>(part + (pw + k + sg) * g.pstride +
+                                                                               t * tw + c4));
+                        }
+                    }
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (pw + k <= last)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            sum[q][e].x += x[k][e].x;
+                            sum[q][e].y += x[k][e].y;
+                            sum[q][e].z += x[k][e].z;
+                            sum[q][e].w += x[k][e].w;
+                        }
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int i = i0 + 32 * e;
+            if (i >= n4) continue;
+            const int t = i / w4, c4 = (i - t * w4) * 4;
+            const int p = p0 + t, col = 256 * c + c4;
+            float4 o = sum[0][e];
+            float *dst;
+            if (g.P == 1) {
+                dst = a.t + (int64_t)p * 2 * a.r + seg_m(g, j) * a.r + col;
+            } else if (g.P == 2) {
+                const float wt = wbd ? load_weight(a.weights, a.w_type, a.rt.order[p]) : 1.f;
+                const float4 u = sum[1][e];
+                o.x = silu_f32(o.x) * u.x * wt;
+                o.y = silu_f32(o.y) * u.y * wt;
+                o.z = silu_f32(o.z) * u.z * wt;
+                o.w = silu_f32(o.w) * u.w * wt;
+                dst = a.h + (int64_t)p * a.f + col;
+            } else if (g.P == 3) {
+                dst = a.s + (int64_t)p * a.r + col;
+            } else {
+                dst = per_slot ? a.out + (int64_t)a.rt.order[p] * a.d + col : a.y + (int64_t)p * a.d + col;
+            }
+            *reinterpret_cast<float4 *>(dst) = o;
+        }
+    }
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) {
+        uint32_t *rdy = a.ready[g.P - 1] + flag_index(g, v, j);
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(rdy), "r"(1u) : "memory");
+    }
+}
+
+// Piece end: the lane-row reduction, the partial-sum slot, the arrival count.
+template <int NT>
+__device__ __forceinline__ void flush_piece(const DecodeArgs &a, const Geo &g, int v, int j, int gw, int lane,
+                                            int rs, int ch, int lpr, bool active, u64 (&acc)[32]) {
+    constexpr int NB = Mode<NT>::NB, COLS = Mode<NT>::COLS;
+    for (int o = lpr; o < 32; o <<= 1) {
+#pragma unroll
+        for (int i = 0; i < NT * NB; ++i) acc[i] = fadd2(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], o));
+    }
+    const int64_t sg = (int64_t)v * g.S + j;
+    const int tw = g.pstride / kNT;
+    if (rs == 0 && active) {
+        float *dst = a.part[g.P - 1] + (gw + sg) * g.pstride + ch * COLS;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int b = 0; b < NB; b += 2) {
+                float x0, x1, x2, x3;
+                unpack2(acc[t * NB + b], x0, x1);
+                unpack2(acc[t * NB + b + 1], x2, x3);
+                *reinterpret_cast<float4 *>(dst + t * tw + 2 * b) = make_float4(x0, x1, x2, x3);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0ull;
+    __threadfence();
+    __syncwarp();
+    uint32_t done = 0;
+    if (lane == 0) {
+        const int fi = flag_index(g, v, j);
+        int target = 0;
+        const int j0 = g.P == 2 ? (j & ~1) : j, nj = g.P == 2 ? 2 : 1;
+        for (int q = 0; q < nj; ++q) target += owner(g, v, j0 + q, g.L / 8 - 1) - owner(g, v, j0 + q, 0) + 1;
+        const uint32_t old = atomicAdd(a.arrive[g.P - 1] + fi, 1u);
+        done = old + 1 == (uint32_t)target;
+    }
+    done = __shfl_sync(0xffffffffu, done, 0);
+    if (done) {
+        __threadfence();
+        finalize(a, g, v, j, lane);
+    }
+}
+
+// Bounded wait (lane 0) for the previous-phase segments holding input rows
+// [row0, row1) of a piece of phase P: phase 2 reads t_m (phase-1 segment
+// (m, c)), phase 3 reads h (phase-2 pair c), phase 4 reads s (phase-3 segment c).
+__device__ void wait_inputs(const DecodeArgs &a, const Geo *geo, int P, int v, int m, int row0, int row1,
+                            int lane) {
+    if (P == 1 || lane != 0) return;
+    const Geo &gp = geo[P - 2];
+    for (int c = row0 / 256; c <= (row1 - 1) / 256; ++c) {
+        const int idx = P == 2 ? v * gp.S + m * gp.C + c : P == 3 ? v * gp.C + c : v * gp.S + c;
+        if (!wait_ge(a.ready[P - 2] + idx, 1u, a.rt.err)) return;
+    }
+}
+
+struct WarpCtx {
+    const Geo *geo;
+    uint8_t *warea;
+    uint32_t wbase, ring, lb;
+    int gw, n_virt, lane;
+};
+
+// Copies INT8 records [first, first + kRecStage) clamped to `end` into the
+// record buffer of parity `par` and commits them as one cp.async group.
+__device__ __forceinline__ void issue_records(const uint8_t *hi, uint32_t first, uint32_t end, uint32_t wbase,
+                                              int par, int lane) {
+    if (hi && first + (uint32_t)lane < end)
+        cp_async16(wbase + kWRec + par * (kRecStage * 16) + lane * 16, hi + (int64_t)(first + lane) * 16);
+    cp_commit();
+}
+
+// One piece: rows [it.row, it.row1) of segment (it.v, it.j) of phase it.P.
+// Per stage k the warp commits the stage's INT8 records (R_k), then the
+// codes of stage k+2 (S_{k+2}); the groups after S_k are always R_{k-1} and
+// S_{k+1}, after R_{k-1} always S_{k+1}, R_k and S_{k+2}.
+template <int NT>
+__device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc, const Iter &it, Issuer &is,
+                                          int &si, int &sc_, int cpc, u64 (&acc)[32]) {
+    constexpr int COLS = Mode<NT>::COLS;
+    const int lane = wc.lane;
+    const Geo &g = wc.geo[it.P - 1];
+    const int P = it.P, v = it.v, j = it.j, row1 = it.row1;
+    const int m = seg_m(g, j), c = seg_c(g, j), w = tile_w(g, c), ng = w >> 5;
+    const int4 ve = __ldg(&a.rt.virt[v]);
+    const int p0 = ve.y;
+    int lpr = 1;
+    while (lpr * COLS < w) lpr <<= 1;
+    const int rps = 32 / lpr, rs = lane / lpr, ch = lane % lpr;
+    const bool active = ch * COLS < w;
+    const int grp = (ch * COLS) >> 5;
+    const latent_qmatrix &qm = phase_matrix(a, P, m);
+    int *tok = reinterpret_cast<int *>(wc.warea + kWTok);
+    if (P == 1 && lane < NT) tok[lane] = a.rt.order[p0 + lane] / a.k;
+    wait_inputs(a, wc.geo, P, v, m, it.row, row1, lane);
+    __syncwarp();
+    const int rl = lane & 15, tq = lane >> 4;
+    float pre[4];
+    load_inputs(a, P, m, p0, NT, it.row + rl, rl < row1 - it.row, tq, tok, pre);
+    const uint8_t *hi = nullptr;
+    uint32_t rec_next = 0, rec_end = 0, prev_mask = 0;
+    int prev_par = -1;
+    const uint8_t *prev_hi = nullptr;
+    for (int row = it.row, k = 0; row < row1; ++k) {
+        const int n = min(kStRows, row1 - row);
+        const int par = k & 1;
+        *reinterpret_cast<float4 *>(wc.warea + kWIn + par * (kStRows * kNT * 4) + rl * (kNT * 4) + tq * 16) =
+            make_float4(pre[0], pre[1], pre[2], pre[3]);
+        if (row + n < row1) load_inputs(a, P, m, p0, NT, row + n + rl, rl < row1 - row - n, tq, tok, pre);
+        cp_wait<2>();  // S_k
+        __syncwarp();
+        if (k == 0 && qm.i8_mask) {  // the piece's INT8 range, from the words issued with S_0
+            const uint32_t *meta = reinterpret_cast<const uint32_t *>(wc.warea + kWMeta + (cpc & 3) * 16);
+            bool past;
+            const int64_t q0 = (int64_t)c * g.L * 8;
+            int8_word(qm, q0 + (int64_t)it.row * ng, past);
+            rec_next = int8_count(meta[0], meta[1], q0 + (int64_t)it.row * ng, past);
+            int8_word(qm, q0 + (int64_t)row1 * ng, past);
+            rec_end = int8_count(meta[2], meta[3], q0 + (int64_t)row1 * ng, past);
+            if (rec_end > rec_next) hi = qm.i8_hi;
+        }
+        issue_records(hi, rec_next, rec_end, wc.wbase, par, lane);  // R_k
+        issue_stage(a, is, wc.warea, wc.geo, wc.gw, wc.n_virt, wc.ring + (si % kRing) * kStBytes, lane);  // S_{k+2}
+        ++si;
+        const uint32_t slot = wc.ring + (sc_ % kRing) * kStBytes;
+        ++sc_;
+        const uint32_t in_s = wc.wbase + kWIn + par * (kStRows * kNT * 4);
+        if (active) stage_rows<NT>(slot, n, w, ng, rs, ch, rps, in_s, wc.lb, acc);
+        uint32_t mask = 0;
+        int crec = 0;
+        if (hi) crec = stage_flags(slot, n, ng, grp, lane, wc.warea, par, mask);
+        if (prev_par >= 0) {  // deferred INT8 pass of stage k-1
+            cp_wait<3>();     // R_{k-1}
+            __syncwarp();
+            if (active && prev_mask) int8_pass<NT>(wc.wbase, prev_par, prev_mask, grp, rs, ch, rps, prev_hi, wc.lb, acc);
+        }
+        prev_par = hi ? par : -1;
+        prev_mask = mask;
+        prev_hi = hi ? hi + (int64_t)rec_next * 16 : nullptr;
+        rec_next += crec;
+        __syncwarp();
+        row += n;
+    }
+    if (prev_par >= 0) {  // INT8 pass of the last stage
+        cp_wait<1>();     // R_last
+        __syncwarp();
+        if (active && prev_mask) int8_pass<NT>(wc.wbase, prev_par, prev_mask, grp, rs, ch, rps, prev_hi, wc.lb, acc);
+        __syncwarp();
+    }
+    flush_piece<NT>(a, g, v, j, wc.gw, lane, rs, ch, lpr, active, acc);
+}
+
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
+    // Device functions take the arguments by reference; a reference to the
+    // kernel parameter would give every thread a local-memory copy, so they
+    // read this shared copy instead.
+    __shared__ DecodeArgs sargs;
+    if (threadIdx.x == 0) sargs = args;
+    const DecodeArgs &a = sargs;
+    extern __shared__ __align__(16) uint8_t dsm[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t a0 = smem_u32(dsm);
+    Geo *geo = reinterpret_cast<Geo *>(dsm);
+    int *cta_nv = reinterpret_cast<int *>(dsm + 4 * sizeof(Geo));
+    uint8_t *table = dsm + (kTableAddr - a0);
+    uint8_t *warea = warp < kLowWarps ? dsm + kCtaBytes + warp * kWarpBytes
+                                      : dsm + (kTableAddr + kTableBytes - a0) + (warp - kLowWarps) * kWarpBytes;
+    static_assert(4 * sizeof(Geo) + 16 <= kCtaBytes, "CTA area");
+    if (a0 > (uint32_t)kMaxSmemBase) {  // layout assumption violated: fail loudly, touch nothing
+        if (threadIdx.x == 0) atomicOr(args.rt.err, kErrLayout);
+        return;
+    }
+    // pair table: entry (tbl, byte e, replica c) at e*256 + tbl*128 + c*8
+    for (int i = threadIdx.x; i < 2 * 256 * 16; i += kSThreads) {
+        const int tbl = i >> 12, e = (i >> 4) & 255, c = i & 15;
+        float lo, hi;
+        if (tbl == 0) {
+            lo = kNF4Levels[e & 15];
+            hi = kNF4Levels[e >> 4];
+        } else {
+            lo = (float)((e & 15) - 8);
+            hi = (float)((e >> 4) - 8);
+        }
+        *reinterpret_cast<float2 *>(table + e * 256 + tbl * 128 + c * 8) = make_float2(lo, hi);
+    }
+    const int G = gridDim.x * kSW, gw = blockIdx.x * kSW + warp;
+    __syncthreads();  // sargs
+    if (threadIdx.x == 0) {
+        const int nv = *a.rt.n_virt;
+        *cta_nv = nv;
+        for (int P = 1; P <= 4; ++P) geo[P - 1] = make_geo(a, P, nv, G);
+    }
+    __syncthreads();
+    WarpCtx wc;
+    wc.geo = geo;
+    wc.warea = warea;
+    wc.wbase = smem_u32(warea);
+    wc.ring = wc.wbase + kWRing;
+    wc.lb = (kTableAddr & 0xFFFF0000u) | (uint32_t)((lane & 15) * 8);
+    wc.gw = gw;
+    wc.n_virt = *cta_nv;
+    wc.lane = lane;
+    Iter *cit = reinterpret_cast<Iter *>(warea + kWIter);
+    if (lane == 0) {
+        Iter z;
+        z.P = 0;
+        z.cur = z.end = Pos{0, 0, 0};
+        z.v = z.j = z.row = z.row1 = 0;
+        *cit = z;
+        *reinterpret_cast<Iter *>(warea + kWIssue) = z;
+    }
+    __syncwarp();
+    Issuer is;
+    is.codes = is.scales = nullptr;
+    is.row = is.row1 = is.cstride = 0;
+    is.P = 0;
+    is.pc = 0;
+    int si = 0, sc_ = 0;  // stages issued / consumed
+    // prologue: E, S_0, E, S_1 (E = empty group standing for R_-2, R_-1)
+    for (int k = 0; k < kRing - 1; ++k, ++si) {
+        cp_commit();
+        issue_stage(a, is, warea, geo, gw, wc.n_virt, wc.ring + (si % kRing) * kStBytes, lane);
+    }
+    u64 acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0ull;
+    Iter it;
+    for (int cpc = 0; shared_iter_next(cit, it, geo, gw, wc.n_virt, lane); ++cpc) {
+        switch (__ldg(&a.rt.virt[it.v].z)) {
+            case 1: run_piece<1>(a, wc, it, is, si, sc_, cpc, acc); break;
+            case 2: run_piece<2>(a, wc, it, is, si, sc_, cpc, acc); break;
+            case 3: run_piece<3>(a, wc, it, is, si, sc_, cpc, acc); break;
+            case 4: run_piece<4>(a, wc, it, is, si, sc_, cpc, acc); break;
+            case 5: run_piece<5>(a, wc, it, is, si, sc_, cpc, acc); break;
+            case 6: run_piece<6>(a, wc, it, is, si, sc_, cpc, acc); break;
+            case 7: run_piece<7>(a, wc, it, is, si, sc_, cpc, acc); break;
+            default: run_piece<8>(a, wc, it, is, si, sc_, cpc, acc); break;
+        }
+    }
+    cp_wait<0>();
+
+    // Phase 5: top-k combine per (token, 256-column tile of d), slot order;
+    // zero rows of tokens without a live slot (of skipped slots with OUT_PER_SLOT).
+    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
+    const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
+    const Geo &g4 = geo[3];
+    const int n_units = (per_slot ? a.T * a.k : a.T) * g4.C;
+    for (int u = gw; u < n_units; u += G) {
+        const int row = u / g4.C, c = u - row * g4.C, w = tile_w(g4, c);
+        const int col = 256 * c + lane * 8;
+        const bool live_col = lane * 8 < w;
+        if (per_slot) {
+            if (a.rt.pos[row] < 0 && live_col) {
+                float4 *o = reinterpret_cast<float4 *>(a.out + (int64_t)row * a.d + col);
+                o[0] = o[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            continue;
+        }
+        float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+        for (int jj = 0; jj < a.k; ++jj) {
+            const int slot = row * a.k + jj;
+            const int p = a.rt.pos[slot];
+            if (p < 0) continue;
+            if (lane == 0) wait_ge(a.ready[3] + a.rt.vslot[p] * g4.C + c, 1u, a.rt.err);
+            __syncwarp();
+            const float wt = wbd ? 1.f : load_weight(a.weights, a.w_type, slot);
+            if (live_col) {
+                const float4 *y = reinterpret_cast<const float4 *>(a.y + (int64_t)p * a.d + col);
+                const float4 y0 = __ldcg(y), y1 = __ldcg(y + 1);
+                s0.x = fmaf(wt, y0.x, s0.x); s0.y = fmaf(wt, y0.y, s0.y);
+                s0.z = fmaf(wt, y0.z, s0.z); s0.w = fmaf(wt, y0.w, s0.w);
+                s1.x = fmaf(wt, y1.x, s1.x); s1.y = fmaf(wt, y1.y, s1.y);
+                s1.z = fmaf(wt, y1.z, s1.z); s1.w = fmaf(wt, y1.w, s1.w);
+            }
+        }
+        if (live_col) {
+            float4 *o = reinterpret_cast<float4 *>(a.out + (int64_t)row * a.d + col);
+            o[0] = s0;
+            o[1] = s1;
+        }
+    }
+}
+
+
+// Host-side mirror of make_geo for sizing (upper bounds over n_virt <= n_virt_max).
+struct HostGeo {
+    int S, C, N, L;
+    int64_t Wv;
+    int pstride;
+};
+
+HostGeo host_geo(const DecodeArgs &a, int P) {
+    HostGeo g;
+    g.L = P == 1 ? a.d : P == 2 ? a.r : P == 3 ? a.f : a.r;
+    g.N = P == 1 ? a.r : P == 2 ? a.f : P == 3 ? a.r : a.d;
+    const int M = P <= 2 ? 2 : 1;
+    g.C = (g.N + 255) / 256;
+    g.S = M * g.C;
+    const int wl = g.N - 256 * (g.C - 1);
+    g.Wv = (int64_t)M * ((int64_t)(g.C - 1) * (g.L / 8) * 8 + (int64_t)(g.L / 8) * (wl / 32));
+    g.pstride = kNT * (g.N < 256 ? g.N : 256);
+    return g;
+}
+
+// Partial-sum slots of phase P: warps used + segments (slot = warp + segment index).
+int64_t host_pieces(const DecodeArgs &a, int P) {
+    const HostGeo g = host_geo(a, P);
+    const int64_t total = g.Wv * a.n_virt_max;
+    int64_t gp = (total + kMinUnits - 1) / kMinUnits;
+    const int64_t G = (int64_t)kMaxCtas * kSW;
+    if (gp > G) gp = G;
+    if (gp < 1) gp = 1;
+    return gp + (int64_t)a.n_virt_max * g.S;
+}
+
+int host_flags(const DecodeArgs &a, int P) {
+    const HostGeo g = host_geo(a, P);
+    return a.n_virt_max * (P == 2 ? g.C : g.S);
 }
 
 }  // namespace
@@ -781,84 +1032,60 @@ const void *pick_decode_fn(int r, int x_type) {
 void decode_plan(DecodeArgs &a) {
     a.R = a.T * a.k;
     a.nmax = a.E < a.R ? a.E : a.R;
-    a.nct_f = (a.f + kTileN - 1) / kTileN;
-    a.nct_d = (a.d + kTileN - 1) / kTileN;
-    plan_split(a.d, a.r, a.kc1, a.ks1);
-    plan_split(a.f, a.r, a.kc2, a.ks2);
-    int in_f = 4 * (a.kc1 > a.kc2 ? a.kc1 : a.kc2);
-    if (in_f < 8 * a.r) in_f = 8 * a.r;
-    a.in_floats = round_up(in_f, 32);
-    const int w = a.r > kTileN ? a.r : kTileN;
-    a.red_floats = (kWarps + 1) * 4 * w;
+    a.n_virt_max = a.nmax + a.R / kVirtTokens + 1;
 }
 
-int decode_sem_count(const DecodeArgs &a) { return 1 + 5 * a.E + a.T * a.nct_d; }
+int decode_sem_count(const DecodeArgs &a) {
+    int n = 0;
+    for (int P = 1; P <= 4; ++P) n += 2 * host_flags(a, P);
+    return n;
+}
 
 size_t decode_scratch_floats(const DecodeArgs &a) {
     const size_t R = (size_t)a.R, r = (size_t)a.r;
-    return (size_t)a.ks1 * R * 2 * r + R * 2 * r + R * (size_t)a.f + (size_t)a.ks2 * R * r + R * r +
-           R * (size_t)a.d + 6 * 64;
+    size_t n = R * 2 * r + R * (size_t)a.f + R * r + R * (size_t)a.d;
+    for (int P = 1; P <= 4; ++P) n += (size_t)host_pieces(a, P) * host_geo(a, P).pstride;
+    return n + 64;
+}
+
+void decode_bind_sem(DecodeArgs &a, uint32_t *sem) {
+    for (int P = 1; P <= 4; ++P) {
+        const int n = host_flags(a, P);
+        a.arrive[P - 1] = sem;
+        sem += n;
+        a.ready[P - 1] = sem;
+        sem += n;
+    }
+}
+
+void decode_bind_scratch(DecodeArgs &a, float *f) {
+    const size_t R = (size_t)a.R, r = (size_t)a.r;
+    a.t = f;  f += R * 2 * r;
+    a.h = f;  f += R * (size_t)a.f;
+    a.s = f;  f += R * r;
+    a.y = f;  f += R * (size_t)a.d;
+    for (int P = 1; P <= 4; ++P) {
+        a.part_pieces[P - 1] = host_pieces(a, P);
+        a.part[P - 1] = f;
+        f += (size_t)a.part_pieces[P - 1] * host_geo(a, P).pstride;
+    }
 }
 
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t s, Marks *marks) {
-    const void *fn = pick_decode_fn(a.r, a.x_type);
-    if (!fn) return cudaErrorInvalidValue;
-    const size_t smem = (size_t)kStages * kStageBytes + kI8Scratch +
-                        (size_t)(a.in_floats + a.red_floats + 4 * kTileN) * sizeof(float);
-    cudaError_t err = ensure_smem(fn, smem);
+    const void *fn = (const void *)k_decode;
+    cudaError_t err = ensure_smem(fn, kDynSmem);
     if (err != cudaSuccess) return err;
     int dev = 0, sms = 0, per_sm = 0;
     if ((err = cudaGetDevice(&dev)) != cudaSuccess) return err;
     if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return err;
-    if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem)) != cudaSuccess) return err;
+    if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kSThreads, kDynSmem)) != cudaSuccess)
+        return err;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    const int grid = sms * per_sm;
+    const int grid = sms < kMaxCtas ? sms : kMaxCtas;
     void *args[] = {(void *)&a};
-    err = cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kThreads), args, smem, s);
+    err = cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kSThreads), args, kDynSmem, s);
     if (marks) marks->mark(s);
     return err;
-}
-
-}  // namespace latent
-
-namespace latent {
-
-namespace {
-
-// Top-k combine of per-routed-row outputs in slot order (used by the
-// expert-parallel return path), or zero rows of skipped slots in per-slot mode.
-__global__ void __launch_bounds__(256) k_combine(DecodeArgs a) {
-    const int t = blockIdx.y;
-    const int c = (blockIdx.x * 256 + threadIdx.x) * 4;
-    if (c >= a.d) return;
-    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
-    const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < a.k; ++j) {
-        const int slot = t * a.k + j;
-        const int p = a.rt.pos[slot];
-        if (per_slot) {
-            if (p < 0) *reinterpret_cast<float4 *>(a.out + (int64_t)slot * a.d + c) = acc;
-            continue;
-        }
-        if (p < 0) continue;
-        const float w = wbd ? 1.f : load_weight(a.weights, a.w_type, slot);
-        const float4 v = *reinterpret_cast<const float4 *>(a.y + (int64_t)p * a.d + c);
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
-    }
-    if (!per_slot) *reinterpret_cast<float4 *>(a.out + (int64_t)t * a.d + c) = acc;
-}
-
-}  // namespace
-
-cudaError_t launch_combine(const DecodeArgs &a, cudaStream_t s) {
-    if (a.T == 0) return cudaSuccess;
-    dim3 grid((a.d / 4 + 255) / 256, a.T);
-    k_combine<<<grid, 256, 0, s>>>(a);
-    return cudaGetLastError();
 }
 
 }  // namespace latent

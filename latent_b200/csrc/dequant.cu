@@ -16,14 +16,15 @@ __global__ void __launch_bounds__(256) k_dequant(latent_qmatrix m, int expert, f
     const int64_t n = (int64_t)M.rows * M.cols;
     const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (i >= n) return;
-    const uint32_t w = __ldg(reinterpret_cast<const uint32_t *>(M.codes + (i >> 1)));
-    const int64_t g = i >> 5;
+    const int row = (int)(i / M.cols), col = (int)(i - (int64_t)row * M.cols);
+    const int64_t g = tile_group(M.rows, M.cols, row, col);
+    const uint32_t w = __ldg(reinterpret_cast<const uint32_t *>(M.codes + g * 16 + ((col & 31) >> 1)));
     const uint16_t sb = __ldg(M.scales + g);
     const float sc = half_bits_to_float(sb & 0x7FFFu);
     float v[8];
     uint32_t idx;
     if ((sb & 0x8000u) && M.i8.present() && M.i8.is_int8(g, &idx)) {
-        const uint32_t hw = __ldg(reinterpret_cast<const uint32_t *>(M.i8.hi + (int64_t)idx * 16 + ((i & 31) >> 1)));
+        const uint32_t hw = __ldg(reinterpret_cast<const uint32_t *>(M.i8.hi + (int64_t)idx * 16 + ((col & 31) >> 1)));
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(int8_elem(w, hw, j), sc);
     } else {

@@ -12,6 +12,7 @@ namespace latent {
 constexpr int kRouteSingleMax = 4096;  // routed slots served by one routing block
 constexpr int kRouteChunk = 8192;      // slots per block in the multi-block routing
 constexpr int kMaxExperts = 1024;
+constexpr int kVirtTokens = 8;         // routed positions per virtual expert (decode path)
 
 struct RouteArgs {
     const int32_t *ids;
@@ -30,6 +31,11 @@ struct RouteArgs {
     int32_t *block_counts;  // [n_blocks][E]
     int chunk;
     int n_blocks;
+    // Virtual experts (decode path only; NULL otherwise): every active expert
+    // split into groups of at most kVirtTokens routed positions, in active order.
+    int4 *virt;       // [n_virt] {expert, first position, positions, 0}
+    int32_t *n_virt;  // [1]
+    int32_t *vslot;   // [R] virtual expert of each routed position
 };
 
 size_t route_block_counts_bytes(int E, int R);
@@ -45,6 +51,9 @@ struct Routing {
     const int32_t *pos;
     uint32_t *sem;
     uint32_t *err;
+    const int4 *virt;
+    const int32_t *n_virt;
+    const int32_t *vslot;
 };
 
 struct DecodeArgs {
@@ -56,26 +65,20 @@ struct DecodeArgs {
     float *out;
     latent_qmatrix gate_a, gate_b, up_a, up_b, down_a, down_b;
     Routing rt;
-    float *part1;  // [ks1][R][2r]
-    float *t;      // [R][2r]
-    float *h;      // [R][f]
-    float *part2;  // [ks2][R][r]
-    float *s;      // [R][r]
-    float *y;      // [R][d]
-    int R;         // T * k
-    int nmax;      // upper bound on active experts: min(E, R)
-    int kc1, ks1;  // rows per split-K chunk / chunks, x -> t
-    int kc2, ks2;  // rows per split-K chunk / chunks, h -> s
-    int nct_f, nct_d;          // 256-column tiles of f and d
-    int in_floats, red_floats;  // shared-memory carve-up of the fused kernel
-    // Counters in the routing block's zeroed region (decode_sem_count of them):
-    uint32_t *work;    // [1] next work item
-    uint32_t *arr1;    // [E] phase-1 chunk arrivals
-    uint32_t *flag1;   // [E] t of the expert is complete
-    uint32_t *cnt2;    // [E] finished phase-2 tiles
-    uint32_t *arr3;    // [E] phase-3 chunk arrivals
-    uint32_t *flag3;   // [E] s of the expert is complete
-    uint32_t *tokcnt;  // [T][nct_d] finished slots per (token, d tile)
+    int R;           // T * k
+    int nmax;        // upper bound on active experts: min(E, R)
+    int n_virt_max;  // upper bound on virtual experts
+    // Per routed position: the reduced outputs of each phase of the decode chain.
+    float *t;  // [R][2r]  x.[A_g | A_u]
+    float *h;  // [R][f]   silu(t_g.B_g) * (t_u.B_u) [* w]
+    float *s;  // [R][r]   h.A_d
+    float *y;  // [R][d]   s.B_d (also the combine input of the prefill and EP paths)
+    // Decode stream: split-K partial sums (one slot per work piece), arrival
+    // counters and ready flags per segment, for phases 1-4.
+    float *part[4];
+    int64_t part_pieces[4];
+    uint32_t *arrive[4];
+    uint32_t *ready[4];
 };
 
 int decode_sem_count(const DecodeArgs &a);
@@ -93,6 +96,10 @@ struct Marks {
 
 void decode_plan(DecodeArgs &a);
 size_t decode_scratch_floats(const DecodeArgs &a);
+// Decode-path counters (zeroed by the routing kernel) and their carve-up.
+void decode_bind_sem(DecodeArgs &a, uint32_t *sem);
+// Carves the decode scratch (decode_scratch_floats floats) into a's buffers.
+void decode_bind_scratch(DecodeArgs &a, float *scratch);
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t s, Marks *marks);
 
 // Prefill path (tcgen05 grouped GEMMs); scratch is prefill_scratch_bytes(a) bytes.

@@ -48,13 +48,12 @@ __global__ void __launch_bounds__(256) k_pf_dequant_t(latent_qmatrix m, __half *
     const QView M = expert_view(m, e);
     const int K = M.rows, N = M.cols;
     const int k0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-    const int64_t gpr = N >> 5;
     {
         const int kk = threadIdx.x >> 2, nn = (threadIdx.x & 3) * 16;
         const int k = k0 + kk, n = n0 + nn;
         if (k < K && n < N) {
-            const uint2 q = __ldg(reinterpret_cast<const uint2 *>(M.codes + (int64_t)k * (N >> 1) + (n >> 1)));
-            const int64_t g = (int64_t)k * gpr + (n >> 5);
+            const int64_t g = tile_group(K, N, k, n);
+            const uint2 q = __ldg(reinterpret_cast<const uint2 *>(M.codes + g * 16 + ((n & 31) >> 1)));
             const uint16_t sb = __ldg(M.scales + g);
             const float sc = half_bits_to_float(sb & 0x7FFFu);
             uint32_t idx;

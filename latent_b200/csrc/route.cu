@@ -6,6 +6,10 @@
 //   order[R]                  flat slot index t*k+j per routed position,
 //                             sorted by expert, then by slot index
 //   pos[T*k]                  routed position of each slot, -1 when skipped
+//   virt[], n_virt, vslot[R]  (decode path) each active expert split into
+//                             virtual experts of <= kVirtTokens consecutive
+//                             routed positions, in active order, and the
+//                             virtual expert of every routed position
 // Slots with id < 0 are skipped (the reference op writes a zero row for
 // them, kernels/latent_fused_expert_ffn.cu:33-40); ids >= E are skipped and
 // flag kErrExpertId.  The same stable order is what the CPU oracle's
@@ -109,6 +113,25 @@ __device__ void block_stable_scatter(const int32_t *ids, int lo, int hi, int E, 
     (void)top_k;
 }
 
+// Virtual-expert table from counts/offsets/active (one block).  nv holds at
+// least E ints of shared scratch; scratch as for block_exclusive_scan.
+__device__ void block_build_virt(const RouteArgs &a, int n_act, int *nv, int *scratch) {
+    const int tid = threadIdx.x;
+    for (int i = tid; i < n_act; i += kRouteThreads) nv[i] = (a.counts[a.active[i]] + kVirtTokens - 1) / kVirtTokens;
+    __syncthreads();
+    const int total = block_exclusive_scan(nv, n_act, scratch);
+    for (int i = tid; i < n_act; i += kRouteThreads) {
+        const int e = a.active[i], ne = a.counts[e], p0 = a.offsets[e];
+        for (int q = 0, v = nv[i]; q * kVirtTokens < ne; ++q, ++v) {
+            const int first = p0 + q * kVirtTokens, n = min(kVirtTokens, ne - q * kVirtTokens);
+            a.virt[v] = make_int4(e, first, n, 0);
+            for (int j = 0; j < n; ++j) a.vslot[first + j] = v;
+        }
+    }
+    if (tid == 0) *a.n_virt = total;
+    __syncthreads();
+}
+
 // One block does everything (small R: decode).
 __global__ void __launch_bounds__(kRouteThreads) k_route_single(RouteArgs a) {
     extern __shared__ int sm[];
@@ -139,6 +162,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_single(RouteArgs a) {
         if (a.counts[i] > 0) a.active[wcnt[i]] = i;
     if (tid == 0) *a.n_active = n_act;
     __syncthreads();
+    if (a.virt) block_build_virt(a, n_act, wcnt, scratch);
     block_stable_scatter(a.ids, 0, a.R, a.E, a.top_k, cnt, wcnt, a.order, a.pos, a.err);
 }
 
@@ -193,6 +217,8 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_scan(RouteArgs a) {
         a.offsets[a.E] = total;
         *a.n_active = n_act;
     }
+    __syncthreads();
+    if (a.virt) block_build_virt(a, n_act, flag, scratch);
 }
 
 // Pass 3: stable scatter within each block from its base offsets.

@@ -16,6 +16,16 @@ gives the ``latent_qmatrix`` of include/latent_ffn.h (codes/scales are the
 concatenation, INT8 groups get a bitmap, per-word base counts and a compact
 ``i8_hi`` table).
 
+On the device every stacked expert matrix is stored in 256-column tile-major
+group order: tile c (columns 256c .. 256c+255, narrower for the last tile)
+holds its rows one after another, each row its w_c/32 groups of 16 code bytes.
+The flat group index q = c*rows*8 + row*(w_c/32) + (col - 256c)/32 addresses
+the codes (16 bytes at 16q), the scale (entry q), the INT8 bitmap bit and the
+order of the compact high-nibble records.  A matrix of at most 256 columns is
+therefore plain row-major.  The order lets a kernel that streams a row range
+of one column tile find its codes, scales and INT8 records as three
+contiguous runs.
+
 Converters accept the reference's NPZ encodings (loader/latent_loader.py:
 NF4 group 32 at :111-145, whole-matrix INT8 group 64 at :148-170) and keep
 every decoded value bit-identical: a reference group that spans 64 elements
@@ -31,6 +41,7 @@ import numpy as np
 import torch
 
 GROUP = 32
+TILE = 256  # columns per device tile
 SCALE_ONE = 0x3C00  # fp16 bits of 1.0
 ZERO_BYTE = 0x77    # two NF4 codes 7 (= 0.0)
 
@@ -166,12 +177,31 @@ def from_npz(arrays: Mapping[str, np.ndarray], name: str, side: str) -> GroupedF
     raise KeyError(f"missing {name}.{side} factor")
 
 
+def tile_order(rows: int, cols: int, device=None) -> torch.Tensor:
+    """Row-major group index of each device (tile-major) group position.
+
+    ``tile_order(rows, cols)[q]`` is the row-major group index (row*cols/32 +
+    col/32) of flat device group q; see the module docstring.
+    """
+    gpr = cols // GROUP
+    parts = []
+    for c0 in range(0, cols, TILE):
+        ng = min(TILE, cols - c0) // GROUP
+        g0 = c0 // GROUP
+        idx = torch.arange(rows, device=device)[:, None] * gpr + g0 + torch.arange(ng, device=device)[None, :]
+        parts.append(idx.reshape(-1))
+    return torch.cat(parts)
+
+
 class StackedFactor:
     """One factor kind of all experts, device-resident, as a ``latent_qmatrix``.
 
-    Tensors: ``codes`` uint8 [E, rows, cols/2], ``scales`` int16 (fp16 bits)
-    [E, rows, cols/32] and, when any group is INT8, ``i8_mask`` / ``i8_base``
-    int32 [E, words] and ``i8_hi`` uint8 [n_int8, 16].
+    Tensors (flat group order q of the module docstring): ``codes`` uint8
+    [E, g, 16], ``scales`` int16 (fp16 bits) [E, g] with g = rows*cols/32,
+    and, when any group is INT8, ``i8_mask`` / ``i8_base`` int32 [E, words]
+    (bit q of expert e's mask marks an INT8 group; base = INT8 groups before
+    the word over all experts) and ``i8_hi`` uint8 [n_int8, 16] in (expert, q)
+    order.
     """
 
     def __init__(self, factors: Sequence[GroupedFactor], device):
@@ -184,12 +214,13 @@ class StackedFactor:
         self.rows, self.cols, self.n_expert = rows, cols, len(factors)
         dev = torch.device(device)
         E, g = len(factors), rows * cols // GROUP
-        self.codes = torch.stack([f.lo.to(dev) for f in factors]).reshape(E, rows, cols // 2).contiguous()
-        is_i8 = torch.stack([f.is_int8.to(dev) for f in factors]).reshape(E, g)
+        perm = tile_order(rows, cols, dev)
+        self.codes = torch.stack([f.lo.to(dev).reshape(g, 16) for f in factors])[:, perm].contiguous()
+        is_i8 = torch.stack([f.is_int8.to(dev).reshape(g) for f in factors])[:, perm]
         # INT8 groups carry the sign bit of their (non-negative) fp16 scale as a flag.
-        sc = torch.stack([f.scales.to(dev) for f in factors]).reshape(E, g)
+        sc = torch.stack([f.scales.to(dev).reshape(g) for f in factors])[:, perm]
         sc = torch.where(is_i8, sc | torch.tensor(-0x8000, dtype=torch.int16, device=dev), sc)
-        self.scales = sc.reshape(E, rows, cols // GROUP).contiguous()
+        self.scales = sc.contiguous()
         self.int8_per_expert = is_i8.sum(dim=1).cpu().tolist()
         self.n_int8 = int(sum(self.int8_per_expert))
         if self.n_int8:
@@ -202,7 +233,7 @@ class StackedFactor:
             per_word = pad.view(E, words, 32).sum(dim=2).reshape(-1)
             base = torch.cumsum(per_word, 0) - per_word
             self.i8_base = base.to(torch.int32).view(E, words).contiguous()
-            hi = torch.stack([f.hi.to(dev) for f in factors]).reshape(E * g, 16)
+            hi = torch.stack([f.hi.to(dev).reshape(g, 16) for f in factors])[:, perm].reshape(E * g, 16)
             self.i8_hi = hi[is_i8.reshape(-1)].contiguous()
         else:
             self.i8_mask = self.i8_base = self.i8_hi = None
@@ -229,21 +260,27 @@ class StackedFactor:
                        self.rows, self.cols)
 
     def expert(self, e: int) -> GroupedFactor:
-        """Copy of expert ``e`` as a GroupedFactor (host side; for tests and tooling)."""
+        """Copy of expert ``e`` as a row-major GroupedFactor (host side; for tests and tooling)."""
         g = self.rows * self.cols // GROUP
-        lo = self.codes[e].reshape(self.rows, self.cols // GROUP, 16).cpu()
-        sc = self.scales[e].cpu() & 0x7FFF
+        perm = tile_order(self.rows, self.cols)
+        lo = torch.empty((g, 16), dtype=torch.uint8)
+        lo[perm] = self.codes[e].cpu()
+        sc = torch.empty(g, dtype=torch.int16)
+        sc[perm] = self.scales[e].cpu() & 0x7FFF
         i8 = torch.zeros(g, dtype=torch.bool)
         hi = torch.zeros((g, 16), dtype=torch.uint8)
         if self.n_int8:
             m = self.i8_mask[e].cpu().to(torch.int64) & 0xFFFFFFFF
             bits = ((m[:, None] >> torch.arange(32)) & 1).reshape(-1)[:g].bool()
-            i8 = bits
             first = int(self.i8_base[e, 0])
             n = int(bits.sum())
-            hi[bits] = self.i8_hi[first:first + n].cpu()
+            hq = torch.zeros((g, 16), dtype=torch.uint8)
+            hq[bits] = self.i8_hi[first:first + n].cpu()
+            hi[perm] = hq
+            i8[perm] = bits
         gpr = self.cols // GROUP
-        return GroupedFactor(self.rows, self.cols, lo, hi.view(self.rows, gpr, 16), sc, i8.view(self.rows, gpr))
+        return GroupedFactor(self.rows, self.cols, lo.view(self.rows, gpr, 16), hi.view(self.rows, gpr, 16),
+                             sc.view(self.rows, gpr), i8.view(self.rows, gpr))
 
 
 KINDS = ("gate_a", "gate_b", "up_a", "up_b", "down_a", "down_b")

@@ -33,7 +33,7 @@ def test_exports_match_header(lib):
 
 
 def test_version_and_status_strings(lib):
-    assert lib.latent_abi_version() == 1
+    assert lib.latent_abi_version() == 2
     assert lib.latent_status_string(0) == b"ok"
     assert b"expert id" in lib.latent_status_string(5)
 

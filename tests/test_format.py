@@ -119,3 +119,44 @@ def test_expert_set_pads_rank_and_counts_bytes():
     per = 3 * (d * 64 + 64 * f) + 3 * 0  # elements per expert... 3 A (rows*64) + 3 B (64*cols)
     elems = 2 * d * 64 + f * 64 + 2 * 64 * f + 64 * d
     assert es.factor_bytes([0]) == elems // 2 + elems // 32 * 2
+
+
+def test_tile_major_order_of_wide_factors():
+    """Factors wider than 256 columns are stored in 256-column tile-major group order."""
+    rng = np.random.default_rng(6)
+    rows, cols = 40, 704  # tiles of 256, 256 and 192 columns
+    fs = []
+    for e in range(2):
+        v = rng.standard_normal((rows, cols)).astype(np.float32)
+        v[:, 5] *= 60  # some INT8 groups
+        fs.append(quantize_factor(torch.from_numpy(v), 20.0))
+    st = F.StackedFactor(fs, "cpu")
+    assert st.n_int8 > 0
+    perm = F.tile_order(rows, cols).numpy()
+    gpr = cols // 32
+    assert perm.shape == (rows * gpr,) and sorted(perm.tolist()) == list(range(rows * gpr))
+    # flat position q of (row, col): tile c, then row, then group within the tile
+    for row, col in ((0, 0), (3, 40), (7, 300), (39, 703), (12, 512)):
+        c = col // 256
+        ng = min(8, gpr - 8 * c)
+        q = c * rows * 8 + row * ng + (col - 256 * c) // 32
+        assert perm[q] == row * gpr + col // 32
+    for e, f in enumerate(fs):
+        lo = f.lo.reshape(-1, 16).numpy()
+        assert np.array_equal(st.codes[e].numpy(), lo[perm])
+        sc = f.scales.reshape(-1).numpy().view(np.uint16)
+        i8 = f.is_int8.reshape(-1).numpy()
+        want = np.where(i8[perm], sc[perm] | 0x8000, sc[perm])
+        assert np.array_equal(st.scales[e].numpy().view(np.uint16), want)
+        back = st.expert(e)
+        assert np.array_equal(_bits(_decode(back)), _bits(_decode(f)))
+    # INT8 records follow the flat order of each expert
+    m = st.i8_mask.numpy().view(np.uint32)
+    bits = ((m[:, :, None].astype(np.uint64) >> np.arange(32, dtype=np.uint64)) & 1).reshape(2, -1)[:, : rows * gpr]
+    first = 0
+    for e, f in enumerate(fs):
+        hi = f.hi.reshape(-1, 16).numpy()[perm]
+        sel = bits[e].astype(bool)
+        n = int(sel.sum())
+        assert np.array_equal(st.i8_hi[first:first + n].numpy(), hi[sel])
+        first += n
