@@ -229,6 +229,16 @@ LATENT_API int latent_dequantize(const latent_qmatrix *m, int32_t expert, float 
 /* y = silu(x) elementwise in fp32 (reference loader/latent_runtime.py:39-45). */
 LATENT_API int latent_silu(const float *x, float *y, int64_t n, struct CUstream_st *stream);
 
+/* Load-time repack of a stacked factor from the row-major layout of the
+ * reference GGUF writer (codes [n_expert][rows][cols/2], fp16 scales
+ * [n_expert][rows][cols/32]; loader/write_latent_gguf.py:101-123) into the
+ * tile-major layout above.  Device buffers, caller-owned, same sizes as the
+ * sources, not overlapping them; 16-byte aligned codes, 2-byte aligned
+ * scales.  Scale sign bits pass through unchanged.  No counterpart in the
+ * reference, whose kernel reads the row-major layout directly. */
+LATENT_API int latent_pack_tiles(const uint8_t *codes, const uint16_t *scales, int32_t n_expert, int64_t rows,
+                                 int64_t cols, uint8_t *dst_codes, uint16_t *dst_scales, struct CUstream_st *stream);
+
 #ifdef __cplusplus
 }
 #endif

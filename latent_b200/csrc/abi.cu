@@ -130,7 +130,7 @@ Layout layout(const latent_ffn_desc *d, const DecodeArgs &a, int path) {
     L.block_counts = o;  o = align_up(o + route_block_counts_bytes((int)E, (int)R));
     const bool dec = path != LATENT_PATH_PREFILL;
     L.virt = o;          o = align_up(o + (dec ? (size_t)a.n_virt_max * 16 : 0));
-    L.n_virt = o;        o = align_up(o + (dec ? 4 : 0));
+    L.n_virt = o;        o = align_up(o + (dec ? 8 : 0));
     L.vslot = o;         o = align_up(o + (dec ? R * 4 : 0));
     L.scratch = o;
     o = align_up(o + (path == LATENT_PATH_PREFILL ? prefill_scratch_bytes(a) : decode_scratch_floats(a) * sizeof(float)));
@@ -386,4 +386,19 @@ extern "C" LATENT_API int latent_dequantize(const latent_qmatrix *m, int32_t exp
 extern "C" LATENT_API int latent_silu(const float *x, float *y, int64_t n, CUstream_st *stream) {
     if (n < 0 || (n > 0 && (!x || !y))) return LATENT_ERR_INVALID;
     return cuda_status(launch_silu(x, y, n, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+extern "C" LATENT_API int latent_pack_tiles(const uint8_t *codes, const uint16_t *scales, int32_t n_expert,
+                                            int64_t rows, int64_t cols, uint8_t *dst_codes, uint16_t *dst_scales,
+                                            CUstream_st *stream) {
+    if (!codes || !scales || !dst_codes || !dst_scales || n_expert < 1) return LATENT_ERR_INVALID;
+    if (rows < 1 || cols < 32 || cols % 32 || rows > (1 << 30) || cols > (1 << 30)) return LATENT_ERR_SHAPE;
+    if (!aligned(codes, 16) || !aligned(dst_codes, 16) || !aligned(scales, 2) || !aligned(dst_scales, 2))
+        return LATENT_ERR_ALIGN;
+    const size_t cb = (size_t)n_expert * rows * cols / 2, sb = (size_t)n_expert * rows * (cols / 32) * 2;
+    const char *c0 = reinterpret_cast<const char *>(codes), *d0 = reinterpret_cast<const char *>(dst_codes);
+    const char *s0 = reinterpret_cast<const char *>(scales), *t0 = reinterpret_cast<const char *>(dst_scales);
+    if ((d0 < c0 + cb && c0 < d0 + cb) || (t0 < s0 + sb && s0 < t0 + sb)) return LATENT_ERR_INVALID;  // overlap
+    return cuda_status(launch_pack_tiles(codes, scales, n_expert, rows, cols, dst_codes, dst_scales,
+                                         reinterpret_cast<cudaStream_t>(stream)));
 }

@@ -48,6 +48,9 @@
 // walks the stage's INT8 records (one contiguous run in the tile-major order;
 // a lane takes its share of the rows of its own group) and adds
 // 16 * (hi' - 8) + 8 through the same table.
+#include <map>
+#include <mutex>
+
 #include "internal.h"
 
 namespace latent {
@@ -87,7 +90,8 @@ constexpr int kWarpBytes = kWIssue + 48;
 static_assert(kWarpBytes % 16 == 0, "warp area alignment");
 // CTA area at the start of dynamic shared memory, then the areas of the low
 // warps, the pair table at shared address 64 K, the remaining warps after it.
-constexpr int kCtaBytes = 512;
+constexpr int kCumCap = 1024;          // virtual experts whose cost prefix is kept in shared memory
+constexpr int kCtaBytes = 512 + (kCumCap + 4) * 4;
 constexpr uint32_t kTableAddr = 65536;
 constexpr int kTableBytes = 65536;
 constexpr int kMaxSmemBase = 4096;      // dynamic shared memory must start below this address
@@ -195,7 +199,19 @@ struct Geo {
     int pstride;  // floats per partial-sum slot: kNT * min(256, N)
     int pad;
     int64_t Uf, Ul, Wm, Wv;  // units of a full tile, the last tile, a matrix, a virtual expert
-    int64_t total;           // units of the phase
+    int64_t total;           // cost-weighted units of the phase: Wv * (sum of the virtual experts' weights)
+};
+
+// Cost-weight prefix of virtual expert v (cum(n_virt) = total weight), from
+// shared memory when it fits there, else from the virtual-expert table.
+struct CumView {
+    const int *s;      // [n + 1] or nullptr
+    const int4 *virt;
+    int n, total;
+    __device__ __forceinline__ int operator()(int v) const {
+        if (s) return s[v];
+        return v >= n ? total : __ldg(&virt[v].w);
+    }
 };
 
 __device__ __forceinline__ int tile_w(const Geo &g, int c) { return c == g.C - 1 ? g.wl : 256; }
@@ -207,7 +223,7 @@ __device__ __forceinline__ int64_t seg_off(const Geo &g, int j) {
     return (int64_t)m * g.Wm + (int64_t)c * g.Uf;
 }
 
-__device__ Geo make_geo(const DecodeArgs &a, int P, int n_virt, int G) {
+__device__ Geo make_geo(const DecodeArgs &a, int P, int n_virt, int wtot, int G) {
     Geo g;
     g.P = P;
     g.L = P == 1 ? a.d : P == 2 ? a.r : P == 3 ? a.f : a.r;
@@ -220,8 +236,8 @@ __device__ Geo make_geo(const DecodeArgs &a, int P, int n_virt, int G) {
     g.Ul = (int64_t)(g.L / 8) * (g.wl / 32);
     g.Wm = (int64_t)(g.C - 1) * g.Uf + g.Ul;
     g.Wv = g.Wm * g.M;
-    g.total = g.Wv * n_virt;
-    const int64_t gp = (g.total + kMinUnits - 1) / kMinUnits;
+    g.total = g.Wv * wtot;
+    const int64_t gp = (g.Wv * n_virt + kMinUnits - 1) / kMinUnits;  // warps used: by bytes, not weights
     g.Gp = (int)(gp < G ? gp : G);
     if (g.Gp < 1) g.Gp = 1;
     g.pstride = kNT * (g.N < 256 ? g.N : 256);
@@ -233,11 +249,17 @@ struct Pos {
     int v, j, blk;
 };
 
-// The block containing unit u (0 <= u < total).
-__device__ Pos pos_of(const Geo &g, int64_t u) {
+// The block containing weighted unit u (0 <= u < total).
+__device__ Pos pos_of(const Geo &g, int64_t u, const CumView &cum) {
     Pos p;
-    p.v = (int)(u / g.Wv);
-    const int64_t rem = u - (int64_t)p.v * g.Wv;
+    int lo = 0, hi = cum.n - 1;  // largest v with cum(v) * Wv <= u
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if ((int64_t)cum(mid) * g.Wv <= u) lo = mid; else hi = mid - 1;
+    }
+    p.v = lo;
+    const int wt = cum(lo + 1) - cum(lo);
+    const int64_t rem = (u - (int64_t)cum(lo) * g.Wv) / wt;
     int c;
     int64_t r3;
     if (g.P == 2) {
@@ -261,10 +283,10 @@ __device__ Pos pos_of(const Geo &g, int64_t u) {
 }
 
 // First block of warp w's range (w in [0, Gp]); warp w owns [start(w), start(w+1)).
-__device__ Pos range_start(const Geo &g, int w, int n_virt) {
+__device__ Pos range_start(const Geo &g, int w, const CumView &cum) {
     const int64_t u = g.total * w / g.Gp;
-    if (u >= g.total) return Pos{n_virt, 0, 0};
-    return pos_of(g, u);
+    if (u >= g.total) return Pos{cum.n, 0, 0};
+    return pos_of(g, u, cum);
 }
 
 __device__ __forceinline__ bool pos_less(const Pos &a, const Pos &b) {
@@ -272,9 +294,10 @@ __device__ __forceinline__ bool pos_less(const Pos &a, const Pos &b) {
 }
 
 // The warp owning block blk of segment (v, j): the last w with start(w) <= block.
-__device__ int owner(const Geo &g, int v, int j, int blk) {
+__device__ int owner(const Geo &g, int v, int j, int blk, const CumView &cum) {
     const int wb = tile_w(g, seg_c(g, j)) / 32;
-    const int64_t end = (int64_t)v * g.Wv + seg_off(g, j) + (int64_t)(blk + 1) * wb;
+    const int c0 = cum(v), wt = cum(v + 1) - c0;
+    const int64_t end = (int64_t)c0 * g.Wv + (int64_t)wt * (seg_off(g, j) + (int64_t)(blk + 1) * wb);
     int w = (int)((end * g.Gp + g.total - 1) / g.total) - 1;
     if (w < 0) w = 0;
     if (w > g.Gp - 1) w = g.Gp - 1;
@@ -294,7 +317,7 @@ struct Iter {
 static_assert(sizeof(Iter) <= 48, "iterator area");
 
 // Moves to the next non-empty piece; false when all phases are done.
-__device__ bool iter_next(Iter &it, const Geo *geo, int gw, int n_virt) {
+__device__ bool iter_next(Iter &it, const Geo *geo, int gw, const CumView &cum) {
     while (true) {
         if (it.P >= 1 && it.P <= 4 && pos_less(it.cur, it.end)) {
             const Geo &g = geo[it.P - 1];
@@ -317,8 +340,8 @@ __device__ bool iter_next(Iter &it, const Geo *geo, int gw, int n_virt) {
         ++it.P;
         const Geo &g = geo[it.P - 1];
         if (gw < g.Gp) {
-            it.cur = range_start(g, gw, n_virt);
-            it.end = range_start(g, gw + 1, n_virt);
+            it.cur = range_start(g, gw, cum);
+            it.end = range_start(g, gw + 1, cum);
         } else {
             it.cur = it.end = Pos{0, 0, 0};
         }
@@ -330,9 +353,10 @@ __device__ __forceinline__ const latent_qmatrix &phase_matrix(const DecodeArgs &
 }
 
 // Iterator step shared by all lanes: load from the warp area, advance, store back.
-__device__ __forceinline__ bool shared_iter_next(Iter *itp, Iter &it, const Geo *geo, int gw, int n_virt, int lane) {
+__device__ __forceinline__ bool shared_iter_next(Iter *itp, Iter &it, const Geo *geo, int gw, const CumView &cum,
+                                                 int lane) {
     it = *itp;
-    const bool more = iter_next(it, geo, gw, n_virt);
+    const bool more = iter_next(it, geo, gw, cum);
     __syncwarp();
     if (lane == 0) *itp = it;
     __syncwarp();
@@ -363,9 +387,9 @@ __device__ __forceinline__ uint32_t int8_count(uint32_t base, uint32_t mask, int
 }
 
 __device__ void issuer_next_piece(const DecodeArgs &a, Issuer &is, uint8_t *warea, const Geo *geo, int gw,
-                                  int n_virt, int lane) {
+                                  const CumView &cum, int lane) {
     Iter it;
-    if (!shared_iter_next(reinterpret_cast<Iter *>(warea + kWIssue), it, geo, gw, n_virt, lane)) {
+    if (!shared_iter_next(reinterpret_cast<Iter *>(warea + kWIssue), it, geo, gw, cum, lane)) {
         is.P = 5;
         return;
     }
@@ -397,8 +421,8 @@ __device__ void issuer_next_piece(const DecodeArgs &a, Issuer &is, uint8_t *ware
 // Issues the next stage into ring slot `slot` (all lanes) and commits one
 // cp.async group (empty once everything is issued).
 __device__ __forceinline__ void issue_stage(const DecodeArgs &a, Issuer &is, uint8_t *warea, const Geo *geo, int gw,
-                                            int n_virt, uint32_t slot, int lane) {
-    if (is.P <= 4 && is.row >= is.row1) issuer_next_piece(a, is, warea, geo, gw, n_virt, lane);
+                                            const CumView &cum, uint32_t slot, int lane) {
+    if (is.P <= 4 && is.row >= is.row1) issuer_next_piece(a, is, warea, geo, gw, cum, lane);
     if (is.P <= 4) {
         const int n = min(kStRows, is.row1 - is.row);
         const int cb = n * is.cstride;  // code bytes, a multiple of 128
@@ -626,83 +650,25 @@ __device__ __forceinline__ int flag_index(const Geo &g, int v, int j) {
     return g.P == 2 ? v * g.C + (j >> 1) : v * g.S + j;
 }
 
-// The piece that completes segment (v, j) (phase 2: the gate/up pair of
-// tile c) sums the partials in piece order and writes the phase output.
-__device__ __noinline__ void finalize(const DecodeArgs &a, const Geo &g, int v, int j, int lane) {
-    const int4 ve = __ldg(&a.rt.virt[v]);
-    const int p0 = ve.y, nt = ve.z;
-    const int c = seg_c(g, j), w = tile_w(g, c), w4 = w >> 2;
-    const int tw = g.pstride / kNT;
-    const float *part = a.part[g.P - 1];
-    const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
-    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
-    const int j0 = g.P == 2 ? (j & ~1) : j, nj = g.P == 2 ? 2 : 1;
-    const int n4 = nt * w4;
-    for (int i0 = lane; i0 < n4; i0 += 128) {
-        float4 sum[2][4];
-        for (int q = 0; q < nj; ++q) {
-            const int64_t sg = (int64_t)v * g.S + j0 + q;
-            const int first = owner(g, v, j0 + q, 0), last = owner(g, v, j0 + q, g.L / 8 - 1);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) sum[q][e] = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int pw = first; pw <= last; pw += 4) {
-                float4 x[4][4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int i = i0 + 32 * e;
-                        x[k][e] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (i < n4 && pw + k <= last) {
-                            const int t = i / w4, c4 = (i - t * w4) * 4;
-                            x[k][e] = __ldcg(reinterpret_cast<const float4 *>(part + (pw + k + sg) * g.pstride +
-                                                                               t * tw + c4));
-                        }
-                    }
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (pw + k <= last)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            sum[q][e].x += x[k][e].x;
-                            sum[q][e].y += x[k][e].y;
-                            sum[q][e].z += x[k][e].z;
-                            sum[q][e].w += x[k][e].w;
-                        }
-            }
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int i = i0 + 32 * e;
-            if (i >= n4) continue;
-            const int t = i / w4, c4 = (i - t * w4) * 4;
-            const int p = p0 + t, col = 256 * c + c4;
-            float4 o = sum[0][e];
-            float *dst;
-            if (g.P == 1) {
-                dst = a.t + (int64_t)p * 2 * a.r + seg_m(g, j) * a.r + col;
-            } else if (g.P == 2) {
-                const float wt = wbd ? load_weight(a.weights, a.w_type, a.rt.order[p]) : 1.f;
-                const float4 u = sum[1][e];
-                o.x = silu_f32(o.x) * u.x * wt;
-                o.y = silu_f32(o.y) * u.y * wt;
-                o.z = silu_f32(o.z) * u.z * wt;
-                o.w = silu_f32(o.w) * u.w * wt;
-                dst = a.h + (int64_t)p * a.f + col;
-            } else if (g.P == 3) {
-                dst = a.s + (int64_t)p * a.r + col;
-            } else {
-                dst = per_slot ? a.out + (int64_t)a.rt.order[p] * a.d + col : a.y + (int64_t)p * a.d + col;
-            }
-            *reinterpret_cast<float4 *>(dst) = o;
-        }
+// Pieces of segment (v, j) of phase P: the warps first..last; for phase 2
+// the gate and up segments of a tile form one reduction group.
+struct SegPieces {
+    int j0, nj;          // first segment of the group, segments in it (1 or 2)
+    int first[2], q[2];  // first piece warp and piece count of each segment
+    int total;           // pieces of the group
+};
+
+__device__ __forceinline__ SegPieces seg_pieces(const Geo &g, int v, int j, const CumView &cum) {
+    SegPieces sp;
+    sp.j0 = g.P == 2 ? (j & ~1) : j;
+    sp.nj = g.P == 2 ? 2 : 1;
+    sp.total = 0;
+    for (int q = 0; q < sp.nj; ++q) {
+        sp.first[q] = owner(g, v, sp.j0 + q, 0, cum);
+        sp.q[q] = owner(g, v, sp.j0 + q, g.L / 8 - 1, cum) - sp.first[q] + 1;
+        sp.total += sp.q[q];
     }
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) {
-        uint32_t *rdy = a.ready[g.P - 1] + flag_index(g, v, j);
-        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(rdy), "r"(1u) : "memory");
-    }
+    return sp;
 }
 
 // Piece end: the lane-row reduction, the partial-sum slot, the arrival count.
@@ -733,19 +699,100 @@ __device__ __forceinline__ void flush_piece(const DecodeArgs &a, const Geo &g, i
     for (int i = 0; i < 32; ++i) acc[i] = 0ull;
     __threadfence();
     __syncwarp();
-    uint32_t done = 0;
-    if (lane == 0) {
-        const int fi = flag_index(g, v, j);
-        int target = 0;
-        const int j0 = g.P == 2 ? (j & ~1) : j, nj = g.P == 2 ? 2 : 1;
-        for (int q = 0; q < nj; ++q) target += owner(g, v, j0 + q, g.L / 8 - 1) - owner(g, v, j0 + q, 0) + 1;
-        const uint32_t old = atomicAdd(a.arrive[g.P - 1] + fi, 1u);
-        done = old + 1 == (uint32_t)target;
+    if (lane == 0) atomicAdd(a.arrive[g.P - 1] + flag_index(g, v, j), 1u);
+}
+
+// One warp's share of the reduction of segment (v, j) (phase 2: of the
+// gate/up pair): once every piece has arrived, the warp sums, in piece
+// order, slice `sl` of the group's output elements and applies the phase
+// epilogue; the last slice to finish sets the ready flag.
+__device__ __noinline__ void reduce_slice(const DecodeArgs &a, const Geo &g, int v, int j, int gw,
+                                          const CumView &cum, int lane) {
+    const SegPieces sp = seg_pieces(g, v, j, cum);
+    const int fi = flag_index(g, v, j);
+    const int sl = (g.P == 2 && (j & 1)) ? sp.q[0] + (gw - sp.first[1]) : gw - sp.first[0];
+    if (lane == 0) wait_ge(a.arrive[g.P - 1] + fi, (uint32_t)sp.total, a.rt.err);
+    __syncwarp();
+    __threadfence();
+    const int4 ve = __ldg(&a.rt.virt[v]);
+    const int p0 = ve.y, nt = ve.z;
+    const int c = seg_c(g, sp.j0), w = tile_w(g, c), w4 = w >> 2;
+    const int tw = g.pstride / kNT;
+    const float *part = a.part[g.P - 1];
+    const int n4 = nt * w4;
+    const int lo = (int)((int64_t)sl * n4 / sp.total), hi = (int)((int64_t)(sl + 1) * n4 / sp.total);
+    const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
+    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
+    for (int i = lo + lane; i < hi; i += 32) {
+        const int t = i / w4, c4 = (i - t * w4) * 4;
+        float4 sum[2];
+        for (int q = 0; q < sp.nj; ++q) {
+            const int64_t sg = (int64_t)v * g.S + sp.j0 + q;
+            const float *base = part + (sg + sp.first[q]) * g.pstride + t * tw + c4;
+            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k = 0; k < sp.q[q]; k += 4) {
+                float4 x[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    x[u] = k + u < sp.q[q] ? __ldcg(reinterpret_cast<const float4 *>(base + (int64_t)(k + u) * g.pstride))
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (k + u < sp.q[q]) {
+                        s.x += x[u].x;
+                        s.y += x[u].y;
+                        s.z += x[u].z;
+                        s.w += x[u].w;
+                    }
+            }
+            sum[q] = s;
+        }
+        const int p = p0 + t, col = 256 * c + c4;
+        float4 o = sum[0];
+        float *dst;
+        if (g.P == 1) {
+            dst = a.t + (int64_t)p * 2 * a.r + seg_m(g, j) * a.r + col;
+        } else if (g.P == 2) {
+            const float wt = wbd ? load_weight(a.weights, a.w_type, a.rt.order[p]) : 1.f;
+            const float4 u = sum[1];
+            o.x = silu_f32(o.x) * u.x * wt;
+            o.y = silu_f32(o.y) * u.y * wt;
+            o.z = silu_f32(o.z) * u.z * wt;
+            o.w = silu_f32(o.w) * u.w * wt;
+            dst = a.h + (int64_t)p * a.f + col;
+        } else if (g.P == 3) {
+            dst = a.s + (int64_t)p * a.r + col;
+        } else {
+            dst = per_slot ? a.out + (int64_t)a.rt.order[p] * a.d + col : a.y + (int64_t)p * a.d + col;
+        }
+        *reinterpret_cast<float4 *>(dst) = o;
     }
-    done = __shfl_sync(0xffffffffu, done, 0);
-    if (done) {
+    __threadfence();
+    __syncwarp();
+    if (lane == 0 && atomicAdd(a.done[g.P - 1] + fi, 1u) + 1 == (uint32_t)sp.total) {
         __threadfence();
-        finalize(a, g, v, j, lane);
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.ready[g.P - 1] + fi), "r"(1u) : "memory");
+    }
+}
+
+// After the warp's range of phase P: its slice of every segment it took a piece of.
+__device__ void reduce_phase(const DecodeArgs &a, const Geo *geo, int P, int gw, const CumView &cum, int lane) {
+    const Geo &g = geo[P - 1];
+    if (gw >= g.Gp) return;
+    Iter it;
+    it.P = P;
+    it.cur = range_start(g, gw, cum);
+    it.end = range_start(g, gw + 1, cum);
+    while (pos_less(it.cur, it.end)) {
+        const int v = it.cur.v, j = it.cur.j;
+        const int row = it.cur.blk * 8;
+        const int row1 = (it.cur.v == it.end.v && it.cur.j == it.end.j) ? it.end.blk * 8 : g.L;
+        if (++it.cur.j == g.S) {
+            it.cur.j = 0;
+            ++it.cur.v;
+        }
+        it.cur.blk = 0;
+        if (row1 > row) reduce_slice(a, g, v, j, gw, cum, lane);
     }
 }
 
@@ -766,7 +813,8 @@ struct WarpCtx {
     const Geo *geo;
     uint8_t *warea;
     uint32_t wbase, ring, lb;
-    int gw, n_virt, lane;
+    int gw, lane;
+    CumView cum;
 };
 
 // Copies INT8 records [first, first + kRecStage) clamped to `end` into the
@@ -828,7 +876,7 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
             if (rec_end > rec_next) hi = qm.i8_hi;
         }
         issue_records(hi, rec_next, rec_end, wc.wbase, par, lane);  // R_k
-        issue_stage(a, is, wc.warea, wc.geo, wc.gw, wc.n_virt, wc.ring + (si % kRing) * kStBytes, lane);  // S_{k+2}
+        issue_stage(a, is, wc.warea, wc.geo, wc.gw, wc.cum, wc.ring + (si % kRing) * kStBytes, lane);  // S_{k+2}
         ++si;
         const uint32_t slot = wc.ring + (sc_ % kRing) * kStBytes;
         ++sc_;
@@ -870,11 +918,12 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t a0 = smem_u32(dsm);
     Geo *geo = reinterpret_cast<Geo *>(dsm);
-    int *cta_nv = reinterpret_cast<int *>(dsm + 4 * sizeof(Geo));
+    int *cta_nv = reinterpret_cast<int *>(dsm + 4 * sizeof(Geo));       // n_virt, total weight
+    int *cta_cum = reinterpret_cast<int *>(dsm + 512);                    // [kCumCap + 1]
     uint8_t *table = dsm + (kTableAddr - a0);
     uint8_t *warea = warp < kLowWarps ? dsm + kCtaBytes + warp * kWarpBytes
                                       : dsm + (kTableAddr + kTableBytes - a0) + (warp - kLowWarps) * kWarpBytes;
-    static_assert(4 * sizeof(Geo) + 16 <= kCtaBytes, "CTA area");
+    static_assert(4 * sizeof(Geo) + 16 <= 512, "CTA area");
     if (a0 > (uint32_t)kMaxSmemBase) {  // layout assumption violated: fail loudly, touch nothing
         if (threadIdx.x == 0) atomicOr(args.rt.err, kErrLayout);
         return;
@@ -894,11 +943,10 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
     }
     const int G = gridDim.x * kSW, gw = blockIdx.x * kSW + warp;
     __syncthreads();  // sargs
-    if (threadIdx.x == 0) {
-        const int nv = *a.rt.n_virt;
-        *cta_nv = nv;
-        for (int P = 1; P <= 4; ++P) geo[P - 1] = make_geo(a, P, nv, G);
-    }
+    const int nv = args.rt.n_virt[0], wtot = args.rt.n_virt[1];
+    if (threadIdx.x < 4) geo[threadIdx.x] = make_geo(a, threadIdx.x + 1, nv, wtot, G);
+    if (nv <= kCumCap)
+        for (int v = threadIdx.x; v <= nv; v += kSThreads) cta_cum[v] = v < nv ? __ldg(&args.rt.virt[v].w) : wtot;
     __syncthreads();
     WarpCtx wc;
     wc.geo = geo;
@@ -907,8 +955,12 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
     wc.ring = wc.wbase + kWRing;
     wc.lb = (kTableAddr & 0xFFFF0000u) | (uint32_t)((lane & 15) * 8);
     wc.gw = gw;
-    wc.n_virt = *cta_nv;
     wc.lane = lane;
+    wc.cum.s = nv <= kCumCap ? cta_cum : nullptr;
+    wc.cum.virt = args.rt.virt;
+    wc.cum.n = nv;
+    wc.cum.total = wtot;
+    (void)cta_nv;
     Iter *cit = reinterpret_cast<Iter *>(warea + kWIter);
     if (lane == 0) {
         Iter z;
@@ -928,13 +980,15 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
     // prologue: E, S_0, E, S_1 (E = empty group standing for R_-2, R_-1)
     for (int k = 0; k < kRing - 1; ++k, ++si) {
         cp_commit();
-        issue_stage(a, is, warea, geo, gw, wc.n_virt, wc.ring + (si % kRing) * kStBytes, lane);
+        issue_stage(a, is, warea, geo, gw, wc.cum, wc.ring + (si % kRing) * kStBytes, lane);
     }
     u64 acc[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) acc[i] = 0ull;
     Iter it;
-    for (int cpc = 0; shared_iter_next(cit, it, geo, gw, wc.n_virt, lane); ++cpc) {
+    int reduced = 0;  // phases whose reductions this warp has done
+    for (int cpc = 0; shared_iter_next(cit, it, geo, gw, wc.cum, lane); ++cpc) {
+        while (reduced + 1 < it.P) reduce_phase(a, geo, ++reduced, gw, wc.cum, lane);
         switch (__ldg(&a.rt.virt[it.v].z)) {
             case 1: run_piece<1>(a, wc, it, is, si, sc_, cpc, acc); break;
             case 2: run_piece<2>(a, wc, it, is, si, sc_, cpc, acc); break;
@@ -946,6 +1000,7 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
             default: run_piece<8>(a, wc, it, is, si, sc_, cpc, acc); break;
         }
     }
+    while (reduced < 4) reduce_phase(a, geo, ++reduced, gw, wc.cum, lane);
     cp_wait<0>();
 
     // Phase 5: top-k combine per (token, 256-column tile of d), slot order;
@@ -1037,7 +1092,7 @@ void decode_plan(DecodeArgs &a) {
 
 int decode_sem_count(const DecodeArgs &a) {
     int n = 0;
-    for (int P = 1; P <= 4; ++P) n += 2 * host_flags(a, P);
+    for (int P = 1; P <= 4; ++P) n += 3 * host_flags(a, P);
     return n;
 }
 
@@ -1052,6 +1107,8 @@ void decode_bind_sem(DecodeArgs &a, uint32_t *sem) {
     for (int P = 1; P <= 4; ++P) {
         const int n = host_flags(a, P);
         a.arrive[P - 1] = sem;
+        sem += n;
+        a.done[P - 1] = sem;
         sem += n;
         a.ready[P - 1] = sem;
         sem += n;
@@ -1075,13 +1132,27 @@ cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t s, Marks *marks) {
     const void *fn = (const void *)k_decode;
     cudaError_t err = ensure_smem(fn, kDynSmem);
     if (err != cudaSuccess) return err;
-    int dev = 0, sms = 0, per_sm = 0;
+    int dev = 0;
     if ((err = cudaGetDevice(&dev)) != cudaSuccess) return err;
-    if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return err;
-    if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kSThreads, kDynSmem)) != cudaSuccess)
-        return err;
-    if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    const int grid = sms < kMaxCtas ? sms : kMaxCtas;
+    // SM count and residency per device, queried once
+    static std::mutex mu;
+    static std::map<int, int> grid_of;
+    int grid = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto f = grid_of.find(dev);
+        if (f != grid_of.end()) {
+            grid = f->second;
+        } else {
+            int sms = 0, per_sm = 0;
+            if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return err;
+            if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kSThreads, kDynSmem)) != cudaSuccess)
+                return err;
+            if (per_sm < 1) return cudaErrorInvalidConfiguration;
+            grid = sms < kMaxCtas ? sms : kMaxCtas;
+            grid_of[dev] = grid;
+        }
+    }
     void *args[] = {(void *)&a};
     err = cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kSThreads), args, kDynSmem, s);
     if (marks) marks->mark(s);

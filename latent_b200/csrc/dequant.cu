@@ -36,6 +36,21 @@ __global__ void __launch_bounds__(256) k_dequant(latent_qmatrix m, int expert, f
     dst[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
+// One thread per group: the 16 code bytes and the scale of row-major group
+// (row, g) go to its tile-major position.
+__global__ void __launch_bounds__(256) k_pack_tiles(const uint8_t *codes, const uint16_t *scales, int64_t rows,
+                                                    int64_t cols, int64_t n_groups, uint8_t *dcodes,
+                                                    uint16_t *dscales) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // global row-major group index
+    if (i >= n_groups) return;
+    const int64_t per = rows * (cols >> 5);
+    const int64_t e = i / per, r = i - e * per;
+    const int row = (int)(r / (cols >> 5)), col = (int)(r - (int64_t)row * (cols >> 5)) * 32;
+    const int64_t q = e * per + tile_group((int)rows, (int)cols, row, col);
+    reinterpret_cast<uint4 *>(dcodes)[q] = __ldg(reinterpret_cast<const uint4 *>(codes) + i);
+    dscales[q] = __ldg(scales + i);
+}
+
 __global__ void __launch_bounds__(256) k_silu(const float *x, float *y, int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = silu_f32(x[i]);
@@ -47,6 +62,14 @@ cudaError_t launch_dequant(const latent_qmatrix &m, int expert, float *out, cuda
     const int64_t n8 = m.rows * m.cols / 8;
     if (n8 == 0) return cudaSuccess;
     k_dequant<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(m, expert, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pack_tiles(const uint8_t *codes, const uint16_t *scales, int n_expert, int64_t rows, int64_t cols,
+                              uint8_t *dcodes, uint16_t *dscales, cudaStream_t s) {
+    const int64_t n = (int64_t)n_expert * rows * (cols / 32);
+    if (n == 0) return cudaSuccess;
+    k_pack_tiles<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(codes, scales, rows, cols, n, dcodes, dscales);
     return cudaGetLastError();
 }
 

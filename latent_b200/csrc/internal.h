@@ -14,6 +14,13 @@ constexpr int kRouteChunk = 8192;      // slots per block in the multi-block rou
 constexpr int kMaxExperts = 1024;
 constexpr int kVirtTokens = 8;         // routed positions per virtual expert (decode path)
 
+// Relative decode cost of one code for a virtual expert of nt tokens (the
+// inner loop spends about one instruction per code on the table lookup, half
+// an instruction per token on the packed FMAs, and a per-row overhead that
+// doubles when a lane covers 8 instead of 16 columns); the decode kernel
+// balances its warps by these weights.
+__host__ __device__ constexpr int virt_weight(int nt) { return nt <= 4 ? 6 + 2 * nt : 10 + 2 * nt; }
+
 struct RouteArgs {
     const int32_t *ids;
     int R;          // T * k slots
@@ -33,8 +40,8 @@ struct RouteArgs {
     int n_blocks;
     // Virtual experts (decode path only; NULL otherwise): every active expert
     // split into groups of at most kVirtTokens routed positions, in active order.
-    int4 *virt;       // [n_virt] {expert, first position, positions, 0}
-    int32_t *n_virt;  // [1]
+    int4 *virt;       // [n_virt] {expert, first position, positions, cost weight before it}
+    int32_t *n_virt;  // [2] virtual experts, total cost weight
     int32_t *vslot;   // [R] virtual expert of each routed position
 };
 
@@ -78,6 +85,7 @@ struct DecodeArgs {
     float *part[4];
     int64_t part_pieces[4];
     uint32_t *arrive[4];
+    uint32_t *done[4];
     uint32_t *ready[4];
 };
 
@@ -126,6 +134,8 @@ cudaError_t launch_ep_gather(const EpArgs &a, cudaStream_t s);
 
 cudaError_t launch_dequant(const latent_qmatrix &m, int expert, float *out, cudaStream_t s);
 cudaError_t launch_silu(const float *x, float *y, int64_t n, cudaStream_t s);
+cudaError_t launch_pack_tiles(const uint8_t *codes, const uint16_t *scales, int n_expert, int64_t rows, int64_t cols,
+                              uint8_t *dcodes, uint16_t *dscales, cudaStream_t s);
 
 // Raises the dynamic shared memory limit of `func` on the current device once.
 cudaError_t ensure_smem(const void *func, size_t bytes);

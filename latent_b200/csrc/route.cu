@@ -113,22 +113,35 @@ __device__ void block_stable_scatter(const int32_t *ids, int lo, int hi, int E, 
     (void)top_k;
 }
 
-// Virtual-expert table from counts/offsets/active (one block).  nv holds at
-// least E ints of shared scratch; scratch as for block_exclusive_scan.
-__device__ void block_build_virt(const RouteArgs &a, int n_act, int *nv, int *scratch) {
+// Virtual-expert table from counts/offsets/active (one block): per active
+// expert ceil(count / kVirtTokens) virtual experts, each with the prefix of
+// the cost weights before it.  nv and wv hold at least E ints of shared
+// scratch each; scratch as for block_exclusive_scan.
+__device__ void block_build_virt(const RouteArgs &a, int n_act, int *nv, int *wv, int *scratch) {
     const int tid = threadIdx.x;
-    for (int i = tid; i < n_act; i += kRouteThreads) nv[i] = (a.counts[a.active[i]] + kVirtTokens - 1) / kVirtTokens;
+    for (int i = tid; i < n_act; i += kRouteThreads) {
+        const int ne = a.counts[a.active[i]];
+        const int full = ne / kVirtTokens, rest = ne - full * kVirtTokens;
+        nv[i] = full + (rest > 0);
+        wv[i] = full * virt_weight(kVirtTokens) + (rest > 0 ? virt_weight(rest) : 0);
+    }
     __syncthreads();
     const int total = block_exclusive_scan(nv, n_act, scratch);
+    const int wtotal = block_exclusive_scan(wv, n_act, scratch);
     for (int i = tid; i < n_act; i += kRouteThreads) {
         const int e = a.active[i], ne = a.counts[e], p0 = a.offsets[e];
+        int wsum = wv[i];
         for (int q = 0, v = nv[i]; q * kVirtTokens < ne; ++q, ++v) {
             const int first = p0 + q * kVirtTokens, n = min(kVirtTokens, ne - q * kVirtTokens);
-            a.virt[v] = make_int4(e, first, n, 0);
-            for (int j = 0; j < n; ++j) a.vslot[first + j] = v;
+            a.virt[v] = make_int4(e, first, n, wsum);
+            wsum += virt_weight(n);
+            for (int jj = 0; jj < n; ++jj) a.vslot[first + jj] = v;
         }
     }
-    if (tid == 0) *a.n_virt = total;
+    if (tid == 0) {
+        a.n_virt[0] = total;
+        a.n_virt[1] = wtotal;
+    }
     __syncthreads();
 }
 
@@ -162,7 +175,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_single(RouteArgs a) {
         if (a.counts[i] > 0) a.active[wcnt[i]] = i;
     if (tid == 0) *a.n_active = n_act;
     __syncthreads();
-    if (a.virt) block_build_virt(a, n_act, wcnt, scratch);
+    if (a.virt) block_build_virt(a, n_act, wcnt, wcnt + a.E, scratch);
     block_stable_scatter(a.ids, 0, a.R, a.E, a.top_k, cnt, wcnt, a.order, a.pos, a.err);
 }
 
@@ -218,7 +231,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_scan(RouteArgs a) {
         *a.n_active = n_act;
     }
     __syncthreads();
-    if (a.virt) block_build_virt(a, n_act, flag, scratch);
+    if (a.virt) block_build_virt(a, n_act, flag, cnt, scratch);
 }
 
 // Pass 3: stable scatter within each block from its base offsets.

@@ -72,6 +72,28 @@ def dequantize(factor, expert: int = 0) -> torch.Tensor:
     return out
 
 
+def pack_tiles(codes: torch.Tensor, scales: torch.Tensor, rows: int, cols: int):
+    """Device repack of row-major stacked factor tensors into the tile-major layout.
+
+    ``codes`` uint8 [E, rows, cols/2] and ``scales`` int16 (fp16 bits)
+    [E, rows, cols/32] on a CUDA device, as the reference GGUF writer stores
+    them (loader/write_latent_gguf.py:101-123); returns new (codes [E, g, 16],
+    scales [E, g]) tensors in the order include/latent_ffn.h describes
+    (latent_pack_tiles).
+    """
+    E = codes.shape[0]
+    codes = codes.contiguous()
+    scales = scales.contiguous()
+    if codes.numel() != E * rows * cols // 2 or scales.numel() != E * rows * cols // 32:
+        raise ValueError("codes/scales do not match [E, rows, cols]")
+    g = rows * cols // 32
+    dc = torch.empty((E, g, 16), dtype=torch.uint8, device=codes.device)
+    ds = torch.empty((E, g), dtype=torch.int16, device=codes.device)
+    _lib.check(_lib.lib().latent_pack_tiles(codes.data_ptr(), scales.data_ptr(), E, rows, cols, dc.data_ptr(),
+                                            ds.data_ptr(), _stream_ptr(codes.device)), "latent_pack_tiles")
+    return dc, ds
+
+
 def _as_device_f32(x, dev) -> Tuple[torch.Tensor, bool]:
     if isinstance(x, np.ndarray) or not torch.is_tensor(x):
         return torch.as_tensor(np.asarray(x, dtype=np.float32)).to(dev), True
