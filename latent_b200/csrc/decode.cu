@@ -4,7 +4,7 @@
 //
 // One persistent, cooperatively launched kernel (one CTA per SM) streams the
 // whole chain.  Routed positions are grouped into virtual experts (an expert
-// and up to 8 of its consecutive routed positions).  For every virtual expert
+// and up to 4 of its consecutive routed positions).  For every virtual expert
 // the chain is four phases of "segments", a segment being one 256-column tile
 // of one factor matrix over all of its rows:
 //   phase 1  t = x . [A_g | A_u]        segments (matrix, tile of r), rows d
@@ -34,8 +34,9 @@
 // and phase boundaries, so the weight stream never waits for a dependency.
 // Inputs and INT8 records of the next stage are prefetched into registers.
 //
-// Inner loop: a lane owns 16 consecutive columns (8 code bytes) of a row when
-// the virtual expert has at most 4 tokens, else 8 columns.  One PRMT builds
+// Inner loop: one code path for every virtual expert (fewer than 4 tokens are
+// zero-padded: one instantiation keeps the hot code in the instruction
+// cache); a lane owns 16 consecutive columns (8 code bytes) of a row.  One PRMT builds
 // the shared-memory address of a code byte's entry in a 64 KB table of float
 // pairs (16 replicas x 256 byte values x 2 tables, replica = lane % 16, so a
 // warp lookup touches every bank exactly twice) and one 64-bit load returns
@@ -71,7 +72,7 @@ constexpr int kStCode = kStRows * 128;  // code bytes per stage (at most)
 constexpr int kStScale = kStRows * 16;  // scale bytes per stage (at most)
 constexpr int kStBytes = kStCode + kStScale;
 constexpr int kRecStage = 32;           // INT8 records per stage staged in shared memory
-constexpr int kNT = kVirtTokens;        // tokens per virtual expert (8)
+constexpr int kNT = kVirtTokens;        // tokens per virtual expert (4)
 constexpr int kMinUnits = 64;           // least work per warp, in (8 rows x 32 columns) units
 constexpr unsigned long long kWaitNs = 2000000000ull;  // a dependency wait gives up after 2 s
 
@@ -158,7 +159,7 @@ __device__ __forceinline__ unsigned long long gtime() {
 // kErrTimeout) when the bound is exceeded or another warp already gave up.
 __device__ bool wait_ge(const uint32_t *flag, uint32_t target, uint32_t *err) {
     const unsigned long long t0 = gtime();
-    unsigned ns = 32;
+    unsigned ns = 256;
     while (true) {
         uint32_t v;
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
@@ -170,8 +171,9 @@ __device__ bool wait_ge(const uint32_t *flag, uint32_t target, uint32_t *err) {
             atomicOr(err, kErrTimeout);
             return false;
         }
+        // long sleeps: a polling warp takes issue slots from the warps still computing
         __nanosleep(ns);
-        if (ns < 256) ns <<= 1;
+        if (ns < 2048) ns <<= 1;
     }
 }
 
@@ -839,7 +841,7 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
     const int P = it.P, v = it.v, j = it.j, row1 = it.row1;
     const int m = seg_m(g, j), c = seg_c(g, j), w = tile_w(g, c), ng = w >> 5;
     const int4 ve = __ldg(&a.rt.virt[v]);
-    const int p0 = ve.y;
+    const int p0 = ve.y, nt = ve.z;  // nt <= NT; tokens nt..NT-1 are zero inputs
     int lpr = 1;
     while (lpr * COLS < w) lpr <<= 1;
     const int rps = 32 / lpr, rs = lane / lpr, ch = lane % lpr;
@@ -847,12 +849,12 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
     const int grp = (ch * COLS) >> 5;
     const latent_qmatrix &qm = phase_matrix(a, P, m);
     int *tok = reinterpret_cast<int *>(wc.warea + kWTok);
-    if (P == 1 && lane < NT) tok[lane] = a.rt.order[p0 + lane] / a.k;
+    if (P == 1 && lane < nt) tok[lane] = a.rt.order[p0 + lane] / a.k;
     wait_inputs(a, wc.geo, P, v, m, it.row, row1, lane);
     __syncwarp();
     const int rl = lane & 15, tq = lane >> 4;
     float pre[4];
-    load_inputs(a, P, m, p0, NT, it.row + rl, rl < row1 - it.row, tq, tok, pre);
+    load_inputs(a, P, m, p0, nt, it.row + rl, rl < row1 - it.row, tq, tok, pre);
     const uint8_t *hi = nullptr;
     uint32_t rec_next = 0, rec_end = 0, prev_mask = 0;
     int prev_par = -1;
@@ -860,9 +862,10 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
     for (int row = it.row, k = 0; row < row1; ++k) {
         const int n = min(kStRows, row1 - row);
         const int par = k & 1;
-        *reinterpret_cast<float4 *>(wc.warea + kWIn + par * (kStRows * kNT * 4) + rl * (kNT * 4) + tq * 16) =
-            make_float4(pre[0], pre[1], pre[2], pre[3]);
-        if (row + n < row1) load_inputs(a, P, m, p0, NT, row + n + rl, rl < row1 - row - n, tq, tok, pre);
+        if (tq * 4 < kNT)  // a row holds kNT tokens: lanes 16..31 carry tokens 4..7 when kNT == 8
+            *reinterpret_cast<float4 *>(wc.warea + kWIn + par * (kStRows * kNT * 4) + rl * (kNT * 4) + tq * 16) =
+                make_float4(pre[0], pre[1], pre[2], pre[3]);
+        if (row + n < row1) load_inputs(a, P, m, p0, nt, row + n + rl, rl < row1 - row - n, tq, tok, pre);
         cp_wait<2>();  // S_k
         __syncwarp();
         if (k == 0 && qm.i8_mask) {  // the piece's INT8 range, from the words issued with S_0
@@ -989,16 +992,7 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
     int reduced = 0;  // phases whose reductions this warp has done
     for (int cpc = 0; shared_iter_next(cit, it, geo, gw, wc.cum, lane); ++cpc) {
         while (reduced + 1 < it.P) reduce_phase(a, geo, ++reduced, gw, wc.cum, lane);
-        switch (__ldg(&a.rt.virt[it.v].z)) {
-            case 1: run_piece<1>(a, wc, it, is, si, sc_, cpc, acc); break;
-            case 2: run_piece<2>(a, wc, it, is, si, sc_, cpc, acc); break;
-            case 3: run_piece<3>(a, wc, it, is, si, sc_, cpc, acc); break;
-            case 4: run_piece<4>(a, wc, it, is, si, sc_, cpc, acc); break;
-            case 5: run_piece<5>(a, wc, it, is, si, sc_, cpc, acc); break;
-            case 6: run_piece<6>(a, wc, it, is, si, sc_, cpc, acc); break;
-            case 7: run_piece<7>(a, wc, it, is, si, sc_, cpc, acc); break;
-            default: run_piece<8>(a, wc, it, is, si, sc_, cpc, acc); break;
-        }
+        run_piece<kNT>(a, wc, it, is, si, sc_, cpc, acc);  // one code path: fewer tokens are zero-padded
     }
     while (reduced < 4) reduce_phase(a, geo, ++reduced, gw, wc.cum, lane);
     cp_wait<0>();

@@ -12,14 +12,13 @@ namespace latent {
 constexpr int kRouteSingleMax = 4096;  // routed slots served by one routing block
 constexpr int kRouteChunk = 8192;      // slots per block in the multi-block routing
 constexpr int kMaxExperts = 1024;
-constexpr int kVirtTokens = 8;         // routed positions per virtual expert (decode path)
+constexpr int kVirtTokens = 4;         // routed positions per virtual expert (decode path)
 
-// Relative decode cost of one code for a virtual expert of nt tokens (the
-// inner loop spends about one instruction per code on the table lookup, half
-// an instruction per token on the packed FMAs, and a per-row overhead that
-// doubles when a lane covers 8 instead of 16 columns); the decode kernel
-// balances its warps by these weights.
-__host__ __device__ constexpr int virt_weight(int nt) { return nt <= 4 ? 6 + 2 * nt : 10 + 2 * nt; }
+// Relative decode cost of a virtual expert of nt tokens; the decode kernel
+// balances its warps by these weights.  Its inner loop runs one code path
+// for up to kVirtTokens tokens (fewer are zero-padded), so the cost per
+// byte does not depend on nt.
+__host__ __device__ constexpr int virt_weight(int nt) { return nt > 0 ? 1 : 0; }
 
 struct RouteArgs {
     const int32_t *ids;
