@@ -453,7 +453,7 @@ __device__ __forceinline__ void stage_rows(uint32_t slot, int n, int w, int ng, 
     constexpr int NB = Mode<NT>::NB, COLS = Mode<NT>::COLS;
     const int wb = w >> 1;
     const int gofs = (ch * COLS) >> 5;
-#pragma unroll 1
+#pragma unroll 2
     for (int row = rs; row < n; row += rps) {
         const uint32_t cb = slot + row * wb + ch * NB;
         uint32_t q[2];
@@ -502,12 +502,19 @@ __device__ __forceinline__ int stage_flags(uint32_t slot, int n, int ng, int g, 
                                            uint32_t &mask) {
     uint32_t flags = 0;
     if (lane < n) {
-        uint16_t *stash = reinterpret_cast<uint16_t *>(warea + kWStash + par * (kStRows * 16) + lane * 16);
-        for (int gg = 0; gg < ng; ++gg) {
-            const uint32_t sb = lds16(slot + kStCode + (lane * ng + gg) * 2);
-            if (sb & 0x8000u) {
-                flags |= 1u << gg;
-                stash[gg] = (uint16_t)sb;
+        uint8_t *stash = warea + kWStash + par * (kStRows * 16) + lane * 16;
+        if (ng == 8) {  // full tile: the row's 8 scales are one 16-byte word; keep them all
+            const float4 f = lds_f4(slot + kStCode + lane * 16);
+            const uint32_t w0 = __float_as_uint(f.x), w1 = __float_as_uint(f.y);
+            const uint32_t w2 = __float_as_uint(f.z), w3 = __float_as_uint(f.w);
+            flags = ((w0 >> 15) & 1u) | ((w0 >> 30) & 2u) | ((w1 >> 13) & 4u) | ((w1 >> 28) & 8u) |
+                    ((w2 >> 11) & 16u) | ((w2 >> 26) & 32u) | ((w3 >> 9) & 64u) | ((w3 >> 24) & 128u);
+            *reinterpret_cast<float4 *>(stash) = f;
+        } else {
+            for (int gg = 0; gg < ng; ++gg) {
+                const uint32_t sb = lds16(slot + kStCode + (lane * ng + gg) * 2);
+                flags |= ((sb >> 15) & 1u) << gg;
+                reinterpret_cast<uint16_t *>(stash)[gg] = (uint16_t)sb;
             }
         }
     }
@@ -524,7 +531,7 @@ __device__ __forceinline__ int stage_flags(uint32_t slot, int n, int ng, int g, 
     mask = 0;
     for (int gg = 0; gg < ng; ++gg) {
         const uint32_t b = __ballot_sync(0xffffffffu, (flags >> gg) & 1u);
-        if (gg == g) mask = b & 0xFFFFu;
+        mask = gg == g ? (b & 0xFFFFu) : mask;
     }
     return __shfl_sync(0xffffffffu, incl, 15);
 }
@@ -550,10 +557,14 @@ __device__ __forceinline__ void int8_pass(uint32_t wbase, int par, uint32_t mask
     float cc[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) cc[t] = 0.f;
-    for (int it = beg; it < end; ++it) {
-        const uint32_t ri = lds16(rowb + row * 2);
+    auto next_row = [&](int r) {
+        const uint32_t rest = r >= 31 ? 0u : mask & (0xFFFFFFFEu << r);
+        return __ffs(rest) - 1;
+    };
+    // the high nibbles (XOR 8), scale and inputs of the record of row r
+    auto fetch = [&](int r, uint32_t (&hw)[2], float &sc, float (&xv)[NT]) {
+        const uint32_t ri = lds16(rowb + r * 2);
         const int idx = (int)(ri & 0xFFu) + __popc((ri >> 8) & ((1u << g) - 1u));
-        uint32_t hw[2];
         if (idx < kRecStage) {
             const uint32_t ra = recb + idx * 16 + colb;
             if constexpr (NB == 8) {
@@ -565,30 +576,30 @@ __device__ __forceinline__ void int8_pass(uint32_t wbase, int par, uint32_t mask
                 hw[1] = 0;
             }
         } else {
-            const uint8_t *p = hi_stage + (int64_t)idx * 16 + colb;
+            const uint8_t *q = hi_stage + (int64_t)idx * 16 + colb;
             if constexpr (NB == 8) {
-                const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p));
+                const uint2 v = __ldg(reinterpret_cast<const uint2 *>(q));
                 hw[0] = v.x;
                 hw[1] = v.y;
             } else {
-                hw[0] = __ldg(reinterpret_cast<const uint32_t *>(p));
+                hw[0] = __ldg(reinterpret_cast<const uint32_t *>(q));
                 hw[1] = 0;
             }
         }
         hw[0] ^= 0x88888888u;
         hw[1] ^= 0x88888888u;
-        const uint32_t sb = lds16(stb + row * 16 + g * 2);
-        const float sc = half_bits_to_float((uint16_t)(sb & 0x7FFFu));
-        const uint32_t xa = inb + (uint32_t)row * (kNT * 4);
-        float xv[8];
-        {
-            const float4 x0 = lds_f4(xa);
-            xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
-            if constexpr (NT > 4) {
-                const float4 x1 = lds_f4(xa + 16);
-                xv[4] = x1.x; xv[5] = x1.y; xv[6] = x1.z; xv[7] = x1.w;
-            }
+        sc = half_bits_to_float((uint16_t)(lds16(stb + r * 16 + g * 2) & 0x7FFFu));
+        const uint32_t xa = inb + (uint32_t)r * (kNT * 4);
+        const float4 x0 = lds_f4(xa);
+        float xt[8] = {x0.x, x0.y, x0.z, x0.w, 0.f, 0.f, 0.f, 0.f};
+        if constexpr (NT > 4) {
+            const float4 x1 = lds_f4(xa + 16);
+            xt[4] = x1.x; xt[5] = x1.y; xt[6] = x1.z; xt[7] = x1.w;
         }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) xv[t] = xt[t];
+    };
+    auto apply = [&](const uint32_t (&hw)[2], float sc, const float (&xv)[NT]) {
         u64 xs[NT];
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
@@ -604,8 +615,17 @@ __device__ __forceinline__ void int8_pass(uint32_t wbase, int par, uint32_t mask
 #pragma unroll
             for (int t = 0; t < NT; ++t) ffma2(acc[t * NB + b], xs[t], vv);
         }
-        const uint32_t rest = row >= 31 ? 0u : mask & (0xFFFFFFFEu << row);
-        row = __ffs(rest) - 1;
+    };
+    for (int it = beg; it < end; it += 2) {  // two records in flight
+        const bool two = it + 1 < end;
+        const int row2 = two ? next_row(row) : row;
+        uint32_t hwa[2], hwb[2];
+        float sca, scb, xa[NT], xb[NT];
+        fetch(row, hwa, sca, xa);
+        fetch(row2, hwb, scb, xb);
+        apply(hwa, sca, xa);
+        if (two) apply(hwb, scb, xb);
+        row = next_row(row2);
     }
     // the "+ 8" of every INT8 group visited, on all of the lane's columns
 #pragma unroll
