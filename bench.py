@@ -238,6 +238,17 @@ def cpu_leg(cfg, es, x, ids, w, seconds: float, min_steps: int = 3):
             "ms_per_step": step * 1e3, "dequant_s": dequant_s}
 
 
+def profiled_traffic(workload):
+    """DRAM bytes per k_decode launch from the committed ncu summary of this workload, else None."""
+    f = ROOT / "profiles" / "k_decode_c1.md"
+    if workload != "c1-v2lite-decode" or not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return int(line.split(":")[1])
+    return None
+
+
 def run_ours(args, world, rank, local):
     from latent_b200 import ExpertFFN
     dev = torch.device("cuda", local)
@@ -312,7 +323,7 @@ def run_ours(args, world, rank, local):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE recipe)",
         "config": config_json(cfg, ids, world, "replicas" if world > 1 else "single GPU"),
         "roofline": {"bound": "hbm", "kernel": PHASES[dom], "achieved": ach, "peak": pk["hbm_gbs"],
-                     "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "traffic": None,
+                     "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "traffic": profiled_traffic(cfg.name),
                      "algorithmic_bytes": op_bytes, "mean_ms": float(phase_ms[dom]),
                      "peak_source": pk["source"]},
         "roofline_op": {"achieved": op_ach, "frac": op_ach / pk["hbm_gbs"], "unit": "GB/s",
