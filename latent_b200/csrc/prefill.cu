@@ -17,8 +17,8 @@
 // accumulators, warps 4-7 drain the other accumulator (tcgen05.ld) and run
 // the epilogue, so the epilogue of tile i overlaps the MMAs of tile i+1.
 // Every mbarrier wait is bounded; on a timeout the kernel records
-// kErrTimeout, drains its TMA loads, frees TMEM and exits.  No TMA load uses
-// cluster multicast.
+// kErrTimeout, drains its TMA loads, frees TMEM and exits.  Every TMA load
+// is a plain per-CTA load into the issuing CTA's own shared memory.
 #include <cuda.h>
 
 #include <mutex>
