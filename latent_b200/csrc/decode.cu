@@ -17,16 +17,17 @@
 // 8-row blocks weighted by their width; each warp of the grid takes one
 // contiguous, equally weighted range of it (no work queue, no CTA-wide
 // synchronisation).  A warp's range covers parts ("pieces") of one or a few
-// segments.  A piece accumulates its rows in registers, writes the partial
-// sums of its columns to a slot of its own and counts itself in on the
-// segment's arrival counter; the piece that completes the count adds all
-// partials of the segment in piece order (bitwise deterministic), applies the
-// phase epilogue (SwiGLU and the optional router weight after phase 2) and
-// sets the segment's ready flag.  A piece of the next phase waits (bounded)
-// for the ready flags of the segments it reads.  Every CTA is resident
-// (cooperative launch) and every warp takes its ranges in phase order, so
-// every wait ends; a wait that exceeds its bound sets kErrTimeout and the
-// kernel runs to completion without waiting further.
+// segments.  A piece accumulates its rows in registers and adds the sums of
+// its columns into the phase output with vector atomic adds (the outputs are
+// zeroed at kernel start, before any piece adds), then counts itself in on
+// the segment's arrival counter.  A piece of the next phase waits (bounded)
+// until every piece of the segments it reads has arrived; the SwiGLU (and
+// the optional router weight) is applied where phase 3 loads its inputs.
+// Every CTA is resident (cooperative launch) and every warp takes its ranges
+// in phase order, so every wait ends; a wait that exceeds its bound sets
+// kErrTimeout and the kernel runs to completion without waiting further.
+// The split-K sums are added in arrival order, so results agree between
+// calls to fp32 rounding, not bitwise.
 //
 // Memory path: each warp streams its codes and scales through a private
 // 3-deep cp.async ring of 16-row stages (2 KB of codes + 256 B of scales at
@@ -177,15 +178,6 @@ __device__ bool wait_ge(const uint32_t *flag, uint32_t target, uint32_t *err) {
     }
 }
 
-// INT8 records of expert e before its flat group q (q may be one past the end).
-__device__ __forceinline__ uint32_t int8_before(const latent_qmatrix &m, int e, int64_t q) {
-    const int64_t groups = m.rows * m.cols / 32, words = (groups + 31) / 32;
-    const uint32_t *mask = m.i8_mask + (int64_t)e * words, *base = m.i8_base + (int64_t)e * words;
-    if (q >= groups) return __ldg(base + words - 1) + __popc(__ldg(mask + words - 1));
-    const int64_t w = q >> 5;
-    return __ldg(base + w) + __popc(__ldg(mask + w) & ((1u << (q & 31)) - 1u));
-}
-
 // ---------------------------------------------------------------------------
 // Phase geometry.  A phase has M matrices (1 or 2) of C column tiles of L
 // rows; segment j is (m = j / C, c = j % C), except in phase 2 where it is
@@ -198,8 +190,7 @@ struct Geo {
     int S;        // segments per virtual expert
     int wl;       // width of the last tile
     int Gp;       // warps the phase is spread over
-    int pstride;  // floats per partial-sum slot: kNT * min(256, N)
-    int pad;
+    int pad[2];
     int64_t Uf, Ul, Wm, Wv;  // units of a full tile, the last tile, a matrix, a virtual expert
     int64_t total;           // cost-weighted units of the phase: Wv * (sum of the virtual experts' weights)
 };
@@ -242,8 +233,7 @@ __device__ Geo make_geo(const DecodeArgs &a, int P, int n_virt, int wtot, int G)
     const int64_t gp = (g.Wv * n_virt + kMinUnits - 1) / kMinUnits;  // warps used: by bytes, not weights
     g.Gp = (int)(gp < G ? gp : G);
     if (g.Gp < 1) g.Gp = 1;
-    g.pstride = kNT * (g.N < 256 ? g.N : 256);
-    g.pad = 0;
+    g.pad[0] = g.pad[1] = 0;
     return g;
 }
 
@@ -645,9 +635,10 @@ __device__ __forceinline__ float load_x(const DecodeArgs &a, int64_t i) {
     }
 }
 
-// Inputs of one stage row for tokens 4*tq .. 4*tq+3 (zero when not live).
+// Inputs of one stage row for tokens 4*tq .. 4*tq+3 (zero when not live);
+// phase 3 forms h = silu(g) * u [* w] from the phase-2 sums.
 __device__ __forceinline__ void load_inputs(const DecodeArgs &a, int P, int m, int p0, int nt, int row, bool live,
-                                            int tq, const int *tok, float (&pre)[4]) {
+                                            int tq, const int *tok, const float (&pw)[4], float (&pre)[4]) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int t = 4 * tq + k;
@@ -659,7 +650,8 @@ __device__ __forceinline__ void load_inputs(const DecodeArgs &a, int P, int m, i
             else if (P == 2)
                 v = __ldcg(a.t + (int64_t)p * 2 * a.r + m * a.r + row);
             else if (P == 3)
-                v = __ldcg(a.h + (int64_t)p * a.f + row);
+                v = silu_f32(__ldcg(a.gu + (int64_t)p * 2 * a.f + row)) * __ldcg(a.gu + (int64_t)p * 2 * a.f + a.f + row) *
+                    pw[k];
             else
                 v = __ldcg(a.s + (int64_t)p * a.r + row);
         }
@@ -667,7 +659,7 @@ __device__ __forceinline__ void load_inputs(const DecodeArgs &a, int P, int m, i
     }
 }
 
-// Index of the arrival counter / ready flag of segment (v, j) of phase P.
+// Index of the arrival counter of segment (v, j) of phase P.
 __device__ __forceinline__ int flag_index(const Geo &g, int v, int j) {
     return g.P == 2 ? v * g.C + (j >> 1) : v * g.S + j;
 }
@@ -693,27 +685,48 @@ __device__ __forceinline__ SegPieces seg_pieces(const Geo &g, int v, int j, cons
     return sp;
 }
 
-// Piece end: the lane-row reduction, the partial-sum slot, the arrival count.
+// Piece end: the lane-row reduction, the vector atomic adds into the phase
+// output (after the kernel-start zeroing is complete), the arrival count.
 template <int NT>
-__device__ __forceinline__ void flush_piece(const DecodeArgs &a, const Geo &g, int v, int j, int gw, int lane,
-                                            int rs, int ch, int lpr, bool active, u64 (&acc)[32]) {
+__device__ __forceinline__ void flush_piece(const DecodeArgs &a, const Geo &g, int v, int j, int p0, int nt, int lane,
+                                            int rs, int ch, int lpr, bool active, bool &zeroed, u64 (&acc)[32]) {
     constexpr int NB = Mode<NT>::NB, COLS = Mode<NT>::COLS;
     for (int o = lpr; o < 32; o <<= 1) {
 #pragma unroll
         for (int i = 0; i < NT * NB; ++i) acc[i] = fadd2(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], o));
     }
-    const int64_t sg = (int64_t)v * g.S + j;
-    const int tw = g.pstride / kNT;
+    if (!zeroed) {
+        if (lane == 0) wait_ge(a.zero_done, gridDim.x, a.rt.err);
+        __syncwarp();
+        zeroed = true;
+    }
     if (rs == 0 && active) {
-        float *dst = a.part[g.P - 1] + (gw + sg) * g.pstride + ch * COLS;
+        const int m = seg_m(g, j), col = 256 * seg_c(g, j) + ch * COLS;
+        float *dst;
+        int64_t ld;
+        if (g.P == 1) {
+            ld = 2 * a.r;
+            dst = a.t + (int64_t)p0 * ld + m * a.r + col;
+        } else if (g.P == 2) {
+            ld = 2 * a.f;
+            dst = a.gu + (int64_t)p0 * ld + m * a.f + col;
+        } else if (g.P == 3) {
+            ld = a.r;
+            dst = a.s + (int64_t)p0 * ld + col;
+        } else {
+            ld = a.d;
+            dst = a.y + (int64_t)p0 * ld + col;
+        }
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
+            if (t < nt) {
 #pragma unroll
-            for (int b = 0; b < NB; b += 2) {
-                float x0, x1, x2, x3;
-                unpack2(acc[t * NB + b], x0, x1);
-                unpack2(acc[t * NB + b + 1], x2, x3);
-                *reinterpret_cast<float4 *>(dst + t * tw + 2 * b) = make_float4(x0, x1, x2, x3);
+                for (int b = 0; b < NB; b += 2) {
+                    float x0, x1, x2, x3;
+                    unpack2(acc[t * NB + b], x0, x1);
+                    unpack2(acc[t * NB + b + 1], x2, x3);
+                    atomicAdd(reinterpret_cast<float4 *>(dst + t * ld + 2 * b), make_float4(x0, x1, x2, x3));
+                }
             }
         }
     }
@@ -724,110 +737,23 @@ __device__ __forceinline__ void flush_piece(const DecodeArgs &a, const Geo &g, i
     if (lane == 0) atomicAdd(a.arrive[g.P - 1] + flag_index(g, v, j), 1u);
 }
 
-// One warp's share of the reduction of segment (v, j) (phase 2: of the
-// gate/up pair): once every piece has arrived, the warp sums, in piece
-// order, slice `sl` of the group's output elements and applies the phase
-// epilogue; the last slice to finish sets the ready flag.
-__device__ __noinline__ void reduce_slice(const DecodeArgs &a, const Geo &g, int v, int j, int gw,
-                                          const CumView &cum, int lane) {
+// Bounded wait (lane 0) until every piece of segment (v, j) of phase g.P
+// (phase 2: of the gate/up pair) has arrived.
+__device__ __forceinline__ bool wait_segment(const DecodeArgs &a, const Geo &g, int v, int j, const CumView &cum) {
     const SegPieces sp = seg_pieces(g, v, j, cum);
-    const int fi = flag_index(g, v, j);
-    const int sl = (g.P == 2 && (j & 1)) ? sp.q[0] + (gw - sp.first[1]) : gw - sp.first[0];
-    if (lane == 0) wait_ge(a.arrive[g.P - 1] + fi, (uint32_t)sp.total, a.rt.err);
-    __syncwarp();
-    __threadfence();
-    const int4 ve = __ldg(&a.rt.virt[v]);
-    const int p0 = ve.y, nt = ve.z;
-    const int c = seg_c(g, sp.j0), w = tile_w(g, c), w4 = w >> 2;
-    const int tw = g.pstride / kNT;
-    const float *part = a.part[g.P - 1];
-    const int n4 = nt * w4;
-    const int lo = (int)((int64_t)sl * n4 / sp.total), hi = (int)((int64_t)(sl + 1) * n4 / sp.total);
-    const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
-    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
-    for (int i = lo + lane; i < hi; i += 32) {
-        const int t = i / w4, c4 = (i - t * w4) * 4;
-        float4 sum[2];
-        for (int q = 0; q < sp.nj; ++q) {
-            const int64_t sg = (int64_t)v * g.S + sp.j0 + q;
-            const float *base = part + (sg + sp.first[q]) * g.pstride + t * tw + c4;
-            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int k = 0; k < sp.q[q]; k += 4) {
-                float4 x[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    x[u] = k + u < sp.q[q] ? __ldcg(reinterpret_cast<const float4 *>(base + (int64_t)(k + u) * g.pstride))
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    if (k + u < sp.q[q]) {
-                        s.x += x[u].x;
-                        s.y += x[u].y;
-                        s.z += x[u].z;
-                        s.w += x[u].w;
-                    }
-            }
-            sum[q] = s;
-        }
-        const int p = p0 + t, col = 256 * c + c4;
-        float4 o = sum[0];
-        float *dst;
-        if (g.P == 1) {
-            dst = a.t + (int64_t)p * 2 * a.r + seg_m(g, j) * a.r + col;
-        } else if (g.P == 2) {
-            const float wt = wbd ? load_weight(a.weights, a.w_type, a.rt.order[p]) : 1.f;
-            const float4 u = sum[1];
-            o.x = silu_f32(o.x) * u.x * wt;
-            o.y = silu_f32(o.y) * u.y * wt;
-            o.z = silu_f32(o.z) * u.z * wt;
-            o.w = silu_f32(o.w) * u.w * wt;
-            dst = a.h + (int64_t)p * a.f + col;
-        } else if (g.P == 3) {
-            dst = a.s + (int64_t)p * a.r + col;
-        } else {
-            dst = per_slot ? a.out + (int64_t)a.rt.order[p] * a.d + col : a.y + (int64_t)p * a.d + col;
-        }
-        *reinterpret_cast<float4 *>(dst) = o;
-    }
-    __threadfence();
-    __syncwarp();
-    if (lane == 0 && atomicAdd(a.done[g.P - 1] + fi, 1u) + 1 == (uint32_t)sp.total) {
-        __threadfence();
-        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.ready[g.P - 1] + fi), "r"(1u) : "memory");
-    }
-}
-
-// After the warp's range of phase P: its slice of every segment it took a piece of.
-__device__ void reduce_phase(const DecodeArgs &a, const Geo *geo, int P, int gw, const CumView &cum, int lane) {
-    const Geo &g = geo[P - 1];
-    if (gw >= g.Gp) return;
-    Iter it;
-    it.P = P;
-    it.cur = range_start(g, gw, cum);
-    it.end = range_start(g, gw + 1, cum);
-    while (pos_less(it.cur, it.end)) {
-        const int v = it.cur.v, j = it.cur.j;
-        const int row = it.cur.blk * 8;
-        const int row1 = (it.cur.v == it.end.v && it.cur.j == it.end.j) ? it.end.blk * 8 : g.L;
-        if (++it.cur.j == g.S) {
-            it.cur.j = 0;
-            ++it.cur.v;
-        }
-        it.cur.blk = 0;
-        if (row1 > row) reduce_slice(a, g, v, j, gw, cum, lane);
-    }
+    return wait_ge(a.arrive[g.P - 1] + flag_index(g, v, j), (uint32_t)sp.total, a.rt.err);
 }
 
 // Bounded wait (lane 0) for the previous-phase segments holding input rows
 // [row0, row1) of a piece of phase P: phase 2 reads t_m (phase-1 segment
 // (m, c)), phase 3 reads h (phase-2 pair c), phase 4 reads s (phase-3 segment c).
 __device__ void wait_inputs(const DecodeArgs &a, const Geo *geo, int P, int v, int m, int row0, int row1,
-                            int lane) {
+                            const CumView &cum, int lane) {
     if (P == 1 || lane != 0) return;
     const Geo &gp = geo[P - 2];
     for (int c = row0 / 256; c <= (row1 - 1) / 256; ++c) {
-        const int idx = P == 2 ? v * gp.S + m * gp.C + c : P == 3 ? v * gp.C + c : v * gp.S + c;
-        if (!wait_ge(a.ready[P - 2] + idx, 1u, a.rt.err)) return;
+        const int j = P == 2 ? m * gp.C + c : P == 3 ? 2 * c : c;
+        if (!wait_segment(a, gp, v, j, cum)) return;
     }
 }
 
@@ -854,7 +780,7 @@ __device__ __forceinline__ void issue_records(const uint8_t *hi, uint32_t first,
 // S_{k+1}, after R_{k-1} always S_{k+1}, R_k and S_{k+2}.
 template <int NT>
 __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc, const Iter &it, Issuer &is,
-                                          int &si, int &sc_, int cpc, u64 (&acc)[32]) {
+                                          int &si, int &sc_, int cpc, bool &zeroed, u64 (&acc)[32]) {
     constexpr int COLS = Mode<NT>::COLS;
     const int lane = wc.lane;
     const Geo &g = wc.geo[it.P - 1];
@@ -870,11 +796,17 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
     const latent_qmatrix &qm = phase_matrix(a, P, m);
     int *tok = reinterpret_cast<int *>(wc.warea + kWTok);
     if (P == 1 && lane < nt) tok[lane] = a.rt.order[p0 + lane] / a.k;
-    wait_inputs(a, wc.geo, P, v, m, it.row, row1, lane);
-    __syncwarp();
     const int rl = lane & 15, tq = lane >> 4;
+    float pw[4] = {1.f, 1.f, 1.f, 1.f};  // phase 3: router weights applied to h
+    if (P == 3 && (a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN)) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (4 * tq + k < nt) pw[k] = load_weight(a.weights, a.w_type, a.rt.order[p0 + 4 * tq + k]);
+    }
+    wait_inputs(a, wc.geo, P, v, m, it.row, row1, wc.cum, lane);
+    __syncwarp();
     float pre[4];
-    load_inputs(a, P, m, p0, nt, it.row + rl, rl < row1 - it.row, tq, tok, pre);
+    load_inputs(a, P, m, p0, nt, it.row + rl, rl < row1 - it.row, tq, tok, pw, pre);
     const uint8_t *hi = nullptr;
     uint32_t rec_next = 0, rec_end = 0, prev_mask = 0;
     int prev_par = -1;
@@ -885,7 +817,7 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
         if (tq * 4 < kNT)  // a row holds kNT tokens: lanes 16..31 carry tokens 4..7 when kNT == 8
             *reinterpret_cast<float4 *>(wc.warea + kWIn + par * (kStRows * kNT * 4) + rl * (kNT * 4) + tq * 16) =
                 make_float4(pre[0], pre[1], pre[2], pre[3]);
-        if (row + n < row1) load_inputs(a, P, m, p0, nt, row + n + rl, rl < row1 - row - n, tq, tok, pre);
+        if (row + n < row1) load_inputs(a, P, m, p0, nt, row + n + rl, rl < row1 - row - n, tq, tok, pw, pre);
         cp_wait<2>();  // S_k
         __syncwarp();
         if (k == 0 && qm.i8_mask) {  // the piece's INT8 range, from the words issued with S_0
@@ -926,7 +858,7 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
         if (active && prev_mask) int8_pass<NT>(wc.wbase, prev_par, prev_mask, grp, rs, ch, rps, prev_hi, wc.lb, acc);
         __syncwarp();
     }
-    flush_piece<NT>(a, g, v, j, wc.gw, lane, rs, ch, lpr, active, acc);
+    flush_piece<NT>(a, g, v, j, p0, nt, lane, rs, ch, lpr, active, zeroed, acc);
 }
 
 // ---------------------------------------------------------------------------
@@ -941,7 +873,6 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t a0 = smem_u32(dsm);
     Geo *geo = reinterpret_cast<Geo *>(dsm);
-    int *cta_nv = reinterpret_cast<int *>(dsm + 4 * sizeof(Geo));       // n_virt, total weight
     int *cta_cum = reinterpret_cast<int *>(dsm + 512);                    // [kCumCap + 1]
     uint8_t *table = dsm + (kTableAddr - a0);
     uint8_t *warea = warp < kLowWarps ? dsm + kCtaBytes + warp * kWarpBytes
@@ -970,7 +901,15 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
     if (threadIdx.x < 4) geo[threadIdx.x] = make_geo(a, threadIdx.x + 1, nv, wtot, G);
     if (nv <= kCumCap)
         for (int v = threadIdx.x; v <= nv; v += kSThreads) cta_cum[v] = v < nv ? __ldg(&args.rt.virt[v].w) : wtot;
+    {   // zero this CTA's share of the phase outputs t, gu, s, y (contiguous)
+        const int64_t n4 = (int64_t)a.R * (3 * a.r + 2 * a.f + a.d) / 4;
+        float4 *z = reinterpret_cast<float4 *>(a.t);
+        for (int64_t i = (int64_t)blockIdx.x * kSThreads + threadIdx.x; i < n4; i += (int64_t)gridDim.x * kSThreads)
+            __stcg(z + i, make_float4(0.f, 0.f, 0.f, 0.f));
+        __threadfence();
+    }
     __syncthreads();
+    if (threadIdx.x == 0) atomicAdd(args.zero_done, 1u);
     WarpCtx wc;
     wc.geo = geo;
     wc.warea = warea;
@@ -983,7 +922,6 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
     wc.cum.virt = args.rt.virt;
     wc.cum.n = nv;
     wc.cum.total = wtot;
-    (void)cta_nv;
     Iter *cit = reinterpret_cast<Iter *>(warea + kWIter);
     if (lane == 0) {
         Iter z;
@@ -1009,16 +947,14 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) acc[i] = 0ull;
     Iter it;
-    int reduced = 0;  // phases whose reductions this warp has done
-    for (int cpc = 0; shared_iter_next(cit, it, geo, gw, wc.cum, lane); ++cpc) {
-        while (reduced + 1 < it.P) reduce_phase(a, geo, ++reduced, gw, wc.cum, lane);
-        run_piece<kNT>(a, wc, it, is, si, sc_, cpc, acc);  // one code path: fewer tokens are zero-padded
-    }
-    while (reduced < 4) reduce_phase(a, geo, ++reduced, gw, wc.cum, lane);
+    bool zeroed = false;  // the kernel-start zeroing is known complete
+    for (int cpc = 0; shared_iter_next(cit, it, geo, gw, wc.cum, lane); ++cpc)
+        run_piece<kNT>(a, wc, it, is, si, sc_, cpc, zeroed, acc);  // one code path: fewer tokens are zero-padded
     cp_wait<0>();
 
     // Phase 5: top-k combine per (token, 256-column tile of d), slot order;
-    // zero rows of tokens without a live slot (of skipped slots with OUT_PER_SLOT).
+    // zero rows of tokens without a live slot.  With OUT_PER_SLOT: y rows
+    // copied to their slots, zero rows for skipped slots.
     const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
     const bool wbd = a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN;
     const Geo &g4 = geo[3];
@@ -1028,9 +964,21 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
         const int col = 256 * c + lane * 8;
         const bool live_col = lane * 8 < w;
         if (per_slot) {
-            if (a.rt.pos[row] < 0 && live_col) {
+            const int p = a.rt.pos[row];
+            float4 y0 = make_float4(0.f, 0.f, 0.f, 0.f), y1 = y0;
+            if (p >= 0) {
+                if (lane == 0) wait_segment(a, g4, a.rt.vslot[p], c, wc.cum);
+                __syncwarp();
+                if (live_col) {
+                    const float4 *y = reinterpret_cast<const float4 *>(a.y + (int64_t)p * a.d + col);
+                    y0 = __ldcg(y);
+                    y1 = __ldcg(y + 1);
+                }
+            }
+            if (live_col) {
                 float4 *o = reinterpret_cast<float4 *>(a.out + (int64_t)row * a.d + col);
-                o[0] = o[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                o[0] = y0;
+                o[1] = y1;
             }
             continue;
         }
@@ -1039,7 +987,7 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
             const int slot = row * a.k + jj;
             const int p = a.rt.pos[slot];
             if (p < 0) continue;
-            if (lane == 0) wait_ge(a.ready[3] + a.rt.vslot[p] * g4.C + c, 1u, a.rt.err);
+            if (lane == 0) wait_segment(a, g4, a.rt.vslot[p], c, wc.cum);
             __syncwarp();
             const float wt = wbd ? 1.f : load_weight(a.weights, a.w_type, slot);
             if (live_col) {
@@ -1061,39 +1009,10 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
 
 
 // Host-side mirror of make_geo for sizing (upper bounds over n_virt <= n_virt_max).
-struct HostGeo {
-    int S, C, N, L;
-    int64_t Wv;
-    int pstride;
-};
-
-HostGeo host_geo(const DecodeArgs &a, int P) {
-    HostGeo g;
-    g.L = P == 1 ? a.d : P == 2 ? a.r : P == 3 ? a.f : a.r;
-    g.N = P == 1 ? a.r : P == 2 ? a.f : P == 3 ? a.r : a.d;
-    const int M = P <= 2 ? 2 : 1;
-    g.C = (g.N + 255) / 256;
-    g.S = M * g.C;
-    const int wl = g.N - 256 * (g.C - 1);
-    g.Wv = (int64_t)M * ((int64_t)(g.C - 1) * (g.L / 8) * 8 + (int64_t)(g.L / 8) * (wl / 32));
-    g.pstride = kNT * (g.N < 256 ? g.N : 256);
-    return g;
-}
-
-// Partial-sum slots of phase P: warps used + segments (slot = warp + segment index).
-int64_t host_pieces(const DecodeArgs &a, int P) {
-    const HostGeo g = host_geo(a, P);
-    const int64_t total = g.Wv * a.n_virt_max;
-    int64_t gp = (total + kMinUnits - 1) / kMinUnits;
-    const int64_t G = (int64_t)kMaxCtas * kSW;
-    if (gp > G) gp = G;
-    if (gp < 1) gp = 1;
-    return gp + (int64_t)a.n_virt_max * g.S;
-}
-
 int host_flags(const DecodeArgs &a, int P) {
-    const HostGeo g = host_geo(a, P);
-    return a.n_virt_max * (P == 2 ? g.C : g.S);
+    const int N = P == 1 ? a.r : P == 2 ? a.f : P == 3 ? a.r : a.d;
+    const int C = (N + 255) / 256, S = (P <= 2 ? 2 : 1) * C;
+    return a.n_virt_max * (P == 2 ? C : S);
 }
 
 }  // namespace
@@ -1105,41 +1024,30 @@ void decode_plan(DecodeArgs &a) {
 }
 
 int decode_sem_count(const DecodeArgs &a) {
-    int n = 0;
-    for (int P = 1; P <= 4; ++P) n += 3 * host_flags(a, P);
+    int n = 1;  // zero_done
+    for (int P = 1; P <= 4; ++P) n += host_flags(a, P);
     return n;
 }
 
 size_t decode_scratch_floats(const DecodeArgs &a) {
     const size_t R = (size_t)a.R, r = (size_t)a.r;
-    size_t n = R * 2 * r + R * (size_t)a.f + R * r + R * (size_t)a.d;
-    for (int P = 1; P <= 4; ++P) n += (size_t)host_pieces(a, P) * host_geo(a, P).pstride;
-    return n + 64;
+    return R * 2 * r + R * 2 * (size_t)a.f + R * r + R * (size_t)a.d + 64;
 }
 
 void decode_bind_sem(DecodeArgs &a, uint32_t *sem) {
     for (int P = 1; P <= 4; ++P) {
-        const int n = host_flags(a, P);
         a.arrive[P - 1] = sem;
-        sem += n;
-        a.done[P - 1] = sem;
-        sem += n;
-        a.ready[P - 1] = sem;
-        sem += n;
+        sem += host_flags(a, P);
     }
+    a.zero_done = sem;
 }
 
 void decode_bind_scratch(DecodeArgs &a, float *f) {
     const size_t R = (size_t)a.R, r = (size_t)a.r;
     a.t = f;  f += R * 2 * r;
-    a.h = f;  f += R * (size_t)a.f;
+    a.gu = f; f += R * 2 * (size_t)a.f;
     a.s = f;  f += R * r;
-    a.y = f;  f += R * (size_t)a.d;
-    for (int P = 1; P <= 4; ++P) {
-        a.part_pieces[P - 1] = host_pieces(a, P);
-        a.part[P - 1] = f;
-        f += (size_t)a.part_pieces[P - 1] * host_geo(a, P).pstride;
-    }
+    a.y = f;
 }
 
 cudaError_t launch_decode(const DecodeArgs &a, cudaStream_t s, Marks *marks) {

@@ -74,18 +74,16 @@ struct DecodeArgs {
     int R;           // T * k
     int nmax;        // upper bound on active experts: min(E, R)
     int n_virt_max;  // upper bound on virtual experts
-    // Per routed position: the reduced outputs of each phase of the decode chain.
-    float *t;  // [R][2r]  x.[A_g | A_u]
-    float *h;  // [R][f]   silu(t_g.B_g) * (t_u.B_u) [* w]
-    float *s;  // [R][r]   h.A_d
-    float *y;  // [R][d]   s.B_d (also the combine input of the prefill and EP paths)
-    // Decode stream: split-K partial sums (one slot per work piece), arrival
-    // counters and ready flags per segment, for phases 1-4.
-    float *part[4];
-    int64_t part_pieces[4];
+    // Per routed position: the outputs of each phase of the decode chain,
+    // contiguous in this order (zeroed by the decode kernel, then summed into).
+    float *t;   // [R][2r]  x.[A_g | A_u]
+    float *gu;  // [R][2f]  t_g.B_g | t_u.B_u
+    float *s;   // [R][r]   h.A_d, h = silu(t_g.B_g) * (t_u.B_u) [* w]
+    float *y;   // [R][d]   s.B_d (also the combine input of the prefill and EP paths)
+    // Decode stream: per-segment arrival counters of phases 1-4, and the count
+    // of CTAs that have zeroed their share of t..y.
     uint32_t *arrive[4];
-    uint32_t *done[4];
-    uint32_t *ready[4];
+    uint32_t *zero_done;
 };
 
 int decode_sem_count(const DecodeArgs &a);
