@@ -85,8 +85,7 @@ constexpr int kWStash = kWIn + 2 * kStRows * kNT * 4;  // x2 uint16 [kStRows][8]
 constexpr int kWRow = kWStash + 2 * kStRows * 8 * 2;   // x2 uint16 [kStRows] INT8 prefix | flags << 8
 constexpr int kWRec = kWRow + 2 * kStRows * 2;    // x2 uint8 [kRecStage][16] INT8 records of the stage
 constexpr int kWMeta = kWRec + 2 * kRecStage * 16;  // 4 x uint32 [4] INT8 table words of upcoming pieces
-constexpr int kWTok = kWMeta + 4 * 16;            // int [kNT] token rows of the piece (phase 1)
-constexpr int kWIter = kWTok + kNT * 4;           // Iter of the consumer
+constexpr int kWIter = kWMeta + 4 * 16;           // Iter of the consumer
 constexpr int kWIssue = kWIter + 48;              // Iter of the stage issuer
 constexpr int kWarpBytes = kWIssue + 48;
 static_assert(kWarpBytes % 16 == 0, "warp area alignment");
@@ -605,8 +604,7 @@ __device__ __forceinline__ void int8_pass(uint32_t wbase, int par, uint32_t mask
 #pragma unroll
             for (int t = 0; t < NT; ++t) ffma2(acc[t * NB + b], xs[t], vv);
         }
-    };
-    for (int it = beg; it < end; it += 2) {  // two records in flight
+    };    for (int it = beg; it < end; it += 2) {  // two records in flight
         const bool two = it + 1 < end;
         const int row2 = two ? next_row(row) : row;
         uint32_t hwa[2], hwb[2];
@@ -627,33 +625,63 @@ __device__ __forceinline__ void int8_pass(uint32_t wbase, int par, uint32_t mask
 }
 
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float load_x(const DecodeArgs &a, int64_t i) {
-    switch (a.x_type) {
-        case LATENT_TYPE_F32: return __ldg(reinterpret_cast<const float *>(a.x) + i);
-        case LATENT_TYPE_F16: return __half2float(__ldg(reinterpret_cast<const __half *>(a.x) + i));
-        default: return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16 *>(a.x) + i));
-    }
-}
 
-// Inputs of one stage row for tokens 4*tq .. 4*tq+3 (zero when not live);
-// phase 3 forms h = silu(g) * u [* w] from the phase-2 sums.
-__device__ __forceinline__ void load_inputs(const DecodeArgs &a, int P, int m, int p0, int nt, int row, bool live,
-                                            int tq, const int *tok, const float (&pw)[4], float (&pre)[4]) {
+// Where the inputs of a piece come from (kept in registers for the piece):
+// token k of the lane's four reads element row of row tok[k] (-1: padded
+// token) of the row-major [*, ld] matrix at base.  Phase 3 reads g at base
+// and u half a row further and forms h = silu(g) * u [* w].
+struct InSrc {
+    const void *base;
+    int tok[4];
+    int ld;
+    int kind;  // 0/1/2: x as f32/f16/bf16 (phase 1), 3: fp32 sums, 4: phase 3
+};
+
+__device__ __forceinline__ InSrc make_insrc(const DecodeArgs &a, int P, int m, int p0, int nt, int tq) {
+    InSrc src;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int t = 4 * tq + k;
+        src.tok[k] = t >= nt ? -1 : P == 1 ? __ldg(&a.rt.order[p0 + t]) / a.k : p0 + t;
+    }
+    if (P == 1) {
+        src.base = a.x;
+        src.ld = a.d;
+        src.kind = a.x_type == LATENT_TYPE_F32 ? 0 : a.x_type == LATENT_TYPE_F16 ? 1 : 2;
+    } else if (P == 2) {
+        src.base = a.t + m * a.r;
+        src.ld = 2 * a.r;
+        src.kind = 3;
+    } else if (P == 3) {
+        src.base = a.gu;
+        src.ld = 2 * a.f;
+        src.kind = 4;
+    } else {
+        src.base = a.s;
+        src.ld = a.r;
+        src.kind = 3;
+    }
+    return src;
+}
+
+// Inputs of one stage row for the lane's four tokens (zero when not live).
+__device__ __forceinline__ void load_inputs(const InSrc &src, int row, bool live, const float (&pw)[4],
+                                            float (&pre)[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
         float v = 0.f;
-        if (live && t < nt) {
-            const int p = p0 + t;
-            if (P == 1)
-                v = load_x(a, (int64_t)tok[t] * a.d + row);
-            else if (P == 2)
-                v = __ldcg(a.t + (int64_t)p * 2 * a.r + m * a.r + row);
-            else if (P == 3)
-                v = silu_f32(__ldcg(a.gu + (int64_t)p * 2 * a.f + row)) * __ldcg(a.gu + (int64_t)p * 2 * a.f + a.f + row) *
-                    pw[k];
-            else
-                v = __ldcg(a.s + (int64_t)p * a.r + row);
+        if (live && src.tok[k] >= 0) {
+            const int64_t i = (int64_t)src.tok[k] * src.ld + row;
+            switch (src.kind) {
+                case 0: v = __ldg(reinterpret_cast<const float *>(src.base) + i); break;
+                case 1: v = __half2float(__ldg(reinterpret_cast<const __half *>(src.base) + i)); break;
+                case 2: v = __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16 *>(src.base) + i)); break;
+                case 3: v = __ldcg(reinterpret_cast<const float *>(src.base) + i); break;
+                default: {
+                    const float *g = reinterpret_cast<const float *>(src.base) + i;
+                    v = silu_f32(__ldcg(g)) * __ldcg(g + (src.ld >> 1)) * pw[k];
+                }
+            }
         }
         pre[k] = v;
     }
@@ -794,9 +822,8 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
     const bool active = ch * COLS < w;
     const int grp = (ch * COLS) >> 5;
     const latent_qmatrix &qm = phase_matrix(a, P, m);
-    int *tok = reinterpret_cast<int *>(wc.warea + kWTok);
-    if (P == 1 && lane < nt) tok[lane] = a.rt.order[p0 + lane] / a.k;
     const int rl = lane & 15, tq = lane >> 4;
+    const InSrc src = make_insrc(a, P, m, p0, nt, tq);
     float pw[4] = {1.f, 1.f, 1.f, 1.f};  // phase 3: router weights applied to h
     if (P == 3 && (a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN)) {
 #pragma unroll
@@ -806,57 +833,60 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
     wait_inputs(a, wc.geo, P, v, m, it.row, row1, wc.cum, lane);
     __syncwarp();
     float pre[4];
-    load_inputs(a, P, m, p0, nt, it.row + rl, rl < row1 - it.row, tq, tok, pw, pre);
+    load_inputs(src, it.row + rl, rl < row1 - it.row, pw, pre);
     const uint8_t *hi = nullptr;
     uint32_t rec_next = 0, rec_end = 0, prev_mask = 0;
     int prev_par = -1;
     const uint8_t *prev_hi = nullptr;
-    for (int row = it.row, k = 0; row < row1; ++k) {
-        const int n = min(kStRows, row1 - row);
+    // One pass of the loop per stage, plus one for the deferred INT8 pass of
+    // the last stage (a single copy of the pass code).
+    for (int row = it.row, k = 0;; ++k) {
+        const bool main = row < row1;
+        if (!main && prev_par < 0) break;
+        const int n = main ? min(kStRows, row1 - row) : 0;
         const int par = k & 1;
-        if (tq * 4 < kNT)  // a row holds kNT tokens: lanes 16..31 carry tokens 4..7 when kNT == 8
-            *reinterpret_cast<float4 *>(wc.warea + kWIn + par * (kStRows * kNT * 4) + rl * (kNT * 4) + tq * 16) =
-                make_float4(pre[0], pre[1], pre[2], pre[3]);
-        if (row + n < row1) load_inputs(a, P, m, p0, nt, row + n + rl, rl < row1 - row - n, tq, tok, pw, pre);
-        cp_wait<2>();  // S_k
-        __syncwarp();
-        if (k == 0 && qm.i8_mask) {  // the piece's INT8 range, from the words issued with S_0
-            const uint32_t *meta = reinterpret_cast<const uint32_t *>(wc.warea + kWMeta + (cpc & 3) * 16);
-            bool past;
-            const int64_t q0 = (int64_t)c * g.L * 8;
-            int8_word(qm, q0 + (int64_t)it.row * ng, past);
-            rec_next = int8_count(meta[0], meta[1], q0 + (int64_t)it.row * ng, past);
-            int8_word(qm, q0 + (int64_t)row1 * ng, past);
-            rec_end = int8_count(meta[2], meta[3], q0 + (int64_t)row1 * ng, past);
-            if (rec_end > rec_next) hi = qm.i8_hi;
-        }
-        issue_records(hi, rec_next, rec_end, wc.wbase, par, lane);  // R_k
-        issue_stage(a, is, wc.warea, wc.geo, wc.gw, wc.cum, wc.ring + (si % kRing) * kStBytes, lane);  // S_{k+2}
-        ++si;
-        const uint32_t slot = wc.ring + (sc_ % kRing) * kStBytes;
-        ++sc_;
-        const uint32_t in_s = wc.wbase + kWIn + par * (kStRows * kNT * 4);
-        if (active) stage_rows<NT>(slot, n, w, ng, rs, ch, rps, in_s, wc.lb, acc);
         uint32_t mask = 0;
         int crec = 0;
-        if (hi) crec = stage_flags(slot, n, ng, grp, lane, wc.warea, par, mask);
+        if (main) {
+            if (tq * 4 < kNT)  // a row holds kNT tokens: lanes 16..31 carry tokens 4..7 when kNT == 8
+                *reinterpret_cast<float4 *>(wc.warea + kWIn + par * (kStRows * kNT * 4) + rl * (kNT * 4) + tq * 16) =
+                    make_float4(pre[0], pre[1], pre[2], pre[3]);
+            if (row + n < row1) load_inputs(src, row + n + rl, rl < row1 - row - n, pw, pre);
+            cp_wait<2>();  // S_k
+            __syncwarp();
+            if (k == 0 && qm.i8_mask) {  // the piece's INT8 range, from the words issued with S_0
+                const uint32_t *meta = reinterpret_cast<const uint32_t *>(wc.warea + kWMeta + (cpc & 3) * 16);
+                bool past;
+                const int64_t q0 = (int64_t)c * g.L * 8;
+                int8_word(qm, q0 + (int64_t)it.row * ng, past);
+                rec_next = int8_count(meta[0], meta[1], q0 + (int64_t)it.row * ng, past);
+                int8_word(qm, q0 + (int64_t)row1 * ng, past);
+                rec_end = int8_count(meta[2], meta[3], q0 + (int64_t)row1 * ng, past);
+                if (rec_end > rec_next) hi = qm.i8_hi;
+            }
+            issue_records(hi, rec_next, rec_end, wc.wbase, par, lane);  // R_k
+            issue_stage(a, is, wc.warea, wc.geo, wc.gw, wc.cum, wc.ring + (si % kRing) * kStBytes, lane);  // S_{k+2}
+            ++si;
+            const uint32_t slot = wc.ring + (sc_ % kRing) * kStBytes;
+            ++sc_;
+            const uint32_t in_s = wc.wbase + kWIn + par * (kStRows * kNT * 4);
+            if (active) stage_rows<NT>(slot, n, w, ng, rs, ch, rps, in_s, wc.lb, acc);
+            if (hi) crec = stage_flags(slot, n, ng, grp, lane, wc.warea, par, mask);
+        }
         if (prev_par >= 0) {  // deferred INT8 pass of stage k-1
-            cp_wait<3>();     // R_{k-1}
+            if (main)
+                cp_wait<3>();  // R_{k-1}
+            else
+                cp_wait<1>();  // R_last
             __syncwarp();
             if (active && prev_mask) int8_pass<NT>(wc.wbase, prev_par, prev_mask, grp, rs, ch, rps, prev_hi, wc.lb, acc);
         }
-        prev_par = hi ? par : -1;
+        prev_par = main && hi ? par : -1;
         prev_mask = mask;
         prev_hi = hi ? hi + (int64_t)rec_next * 16 : nullptr;
         rec_next += crec;
         __syncwarp();
         row += n;
-    }
-    if (prev_par >= 0) {  // INT8 pass of the last stage
-        cp_wait<1>();     // R_last
-        __syncwarp();
-        if (active && prev_mask) int8_pass<NT>(wc.wbase, prev_par, prev_mask, grp, rs, ch, rps, prev_hi, wc.lb, acc);
-        __syncwarp();
     }
     flush_piece<NT>(a, g, v, j, p0, nt, lane, rs, ch, lpr, active, zeroed, acc);
 }
