@@ -240,7 +240,8 @@ struct Pos {
     int v, j, blk;
 };
 
-// The block containing weighted unit u (0 <= u < total).
+// The block containing weighted unit u (0 <= u < total).  Offsets inside one
+// virtual expert (< Wv * weight, far below 2^31) use 32-bit arithmetic.
 __device__ Pos pos_of(const Geo &g, int64_t u, const CumView &cum) {
     Pos p;
     int lo = 0, hi = cum.n - 1;  // largest v with cum(v) * Wv <= u
@@ -250,26 +251,28 @@ __device__ Pos pos_of(const Geo &g, int64_t u, const CumView &cum) {
     }
     p.v = lo;
     const int wt = cum(lo + 1) - cum(lo);
-    const int64_t rem = (u - (int64_t)cum(lo) * g.Wv) / wt;
-    int c;
-    int64_t r3;
+    const int rem0 = (int)(u - (int64_t)cum(lo) * g.Wv);
+    const int rem = wt == 1 ? rem0 : rem0 / wt;
+    const int Uf = (int)g.Uf, Ul = (int)g.Ul;
+    int c, r3;
     if (g.P == 2) {
-        c = (int)(rem / (2 * g.Uf));
+        c = rem / (2 * Uf);
         if (c > g.C - 1) c = g.C - 1;
-        const int64_t r2 = rem - (int64_t)c * 2 * g.Uf;
-        const int64_t U = c == g.C - 1 ? g.Ul : g.Uf;
-        const int m = (int)(r2 / U);
+        const int r2 = rem - c * 2 * Uf;
+        const int U = c == g.C - 1 ? Ul : Uf;
+        const int m = r2 / U;
         r3 = r2 - m * U;
         p.j = 2 * c + m;
     } else {
-        const int m = (int)(rem / g.Wm);
-        const int64_t r2 = rem - (int64_t)m * g.Wm;
-        c = (int)(r2 / g.Uf);
+        const int Wm = (int)g.Wm;
+        const int m = rem / Wm;
+        const int r2 = rem - m * Wm;
+        c = r2 / Uf;
         if (c > g.C - 1) c = g.C - 1;
-        r3 = r2 - (int64_t)c * g.Uf;
+        r3 = r2 - c * Uf;
         p.j = m * g.C + c;
     }
-    p.blk = (int)(r3 / (tile_w(g, c) / 32));
+    p.blk = r3 / (tile_w(g, c) / 32);
     return p;
 }
 
@@ -442,7 +445,7 @@ __device__ __forceinline__ void stage_rows(uint32_t slot, int n, int w, int ng, 
     constexpr int NB = Mode<NT>::NB, COLS = Mode<NT>::COLS;
     const int wb = w >> 1;
     const int gofs = (ch * COLS) >> 5;
-#pragma unroll 2
+#pragma unroll 1
     for (int row = rs; row < n; row += rps) {
         const uint32_t cb = slot + row * wb + ch * NB;
         uint32_t q[2];
@@ -664,26 +667,38 @@ __device__ __forceinline__ InSrc make_insrc(const DecodeArgs &a, int P, int m, i
     return src;
 }
 
-// Inputs of one stage row for the lane's four tokens (zero when not live).
-__device__ __forceinline__ void load_inputs(const InSrc &src, int row, bool live, const float (&pw)[4],
-                                            float (&pre)[4]) {
+// Inputs of one stage row for the lane's four tokens (zero when not live),
+// as raw bits (and phase 3's u): the loads complete while the stage before
+// is processed, and in_value converts them when they are stored.
+__device__ __forceinline__ void load_inputs(const InSrc &src, int row, bool live, uint32_t (&raw)[4],
+                                            float (&rawu)[4]) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        float v = 0.f;
+        uint32_t v = 0;
+        float u = 0.f;
         if (live && src.tok[k] >= 0) {
             const int64_t i = (int64_t)src.tok[k] * src.ld + row;
-            switch (src.kind) {
-                case 0: v = __ldg(reinterpret_cast<const float *>(src.base) + i); break;
-                case 1: v = __half2float(__ldg(reinterpret_cast<const __half *>(src.base) + i)); break;
-                case 2: v = __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16 *>(src.base) + i)); break;
-                case 3: v = __ldcg(reinterpret_cast<const float *>(src.base) + i); break;
-                default: {
-                    const float *g = reinterpret_cast<const float *>(src.base) + i;
-                    v = silu_f32(__ldcg(g)) * __ldcg(g + (src.ld >> 1)) * pw[k];
-                }
+            if (src.kind == 1 || src.kind == 2) {
+                v = __ldg(reinterpret_cast<const unsigned short *>(src.base) + i);
+            } else if (src.kind == 0) {
+                v = __ldg(reinterpret_cast<const uint32_t *>(src.base) + i);
+            } else {
+                const uint32_t *g = reinterpret_cast<const uint32_t *>(src.base) + i;
+                v = __ldcg(g);
+                if (src.kind == 4) u = __uint_as_float(__ldcg(g + (src.ld >> 1)));
             }
         }
-        pre[k] = v;
+        raw[k] = v;
+        rawu[k] = u;
+    }
+}
+
+__device__ __forceinline__ float in_value(int kind, uint32_t v, float u, float w) {
+    switch (kind) {
+        case 1: return __half2float(__ushort_as_half((unsigned short)v));
+        case 2: return __uint_as_float(v << 16);  // bf16 -> f32
+        case 4: return silu_f32(__uint_as_float(v)) * u * w;
+        default: return __uint_as_float(v);
     }
 }
 
@@ -832,8 +847,9 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
     }
     wait_inputs(a, wc.geo, P, v, m, it.row, row1, wc.cum, lane);
     __syncwarp();
-    float pre[4];
-    load_inputs(src, it.row + rl, rl < row1 - it.row, pw, pre);
+    uint32_t pre[4];
+    float preu[4];
+    load_inputs(src, it.row + rl, rl < row1 - it.row, pre, preu);
     const uint8_t *hi = nullptr;
     uint32_t rec_next = 0, rec_end = 0, prev_mask = 0;
     int prev_par = -1;
@@ -850,8 +866,9 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
         if (main) {
             if (tq * 4 < kNT)  // a row holds kNT tokens: lanes 16..31 carry tokens 4..7 when kNT == 8
                 *reinterpret_cast<float4 *>(wc.warea + kWIn + par * (kStRows * kNT * 4) + rl * (kNT * 4) + tq * 16) =
-                    make_float4(pre[0], pre[1], pre[2], pre[3]);
-            if (row + n < row1) load_inputs(src, row + n + rl, rl < row1 - row - n, pw, pre);
+                    make_float4(in_value(src.kind, pre[0], preu[0], pw[0]), in_value(src.kind, pre[1], preu[1], pw[1]),
+                                in_value(src.kind, pre[2], preu[2], pw[2]), in_value(src.kind, pre[3], preu[3], pw[3]));
+            if (row + n < row1) load_inputs(src, row + n + rl, rl < row1 - row - n, pre, preu);
             cp_wait<2>();  // S_k
             __syncwarp();
             if (k == 0 && qm.i8_mask) {  // the piece's INT8 range, from the words issued with S_0
