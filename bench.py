@@ -307,7 +307,10 @@ def run_ours(args, world, rank, local):
     e2e_ms = allreduce_max(statistics.mean(a.elapsed_time(b) for a, b in e2e_ev), world)
     ref_out = op(x, ids, w)
     torch.cuda.synchronize()
-    assert torch.equal(hout, ref_out.cpu()), "e2e output differs from the device-resident run"
+    # split-K sums are added in arrival order: the two runs agree to fp32 rounding
+    ref_cpu = ref_out.cpu().double()
+    e2e_rel = float(torch.linalg.vector_norm(hout.double() - ref_cpu) / torch.linalg.vector_norm(ref_cpu))
+    assert e2e_rel <= 1e-6, f"e2e output differs from the device-resident run (rel {e2e_rel:.2e})"
 
     pk = peaks()
     x_bytes = x.numel() * x.element_size()
