@@ -37,7 +37,10 @@
 //
 // Inner loop: one code path for every virtual expert (fewer than 4 tokens are
 // zero-padded: one instantiation keeps the hot code in the instruction
-// cache); a lane owns 16 consecutive columns (8 code bytes) of a row.  One PRMT builds
+// cache); a lane owns 8 consecutive columns (4 code bytes) of a row, which
+// keeps the accumulators at 32 registers and lets 16 warps share an SM (the
+// kernel is latency-bound: more warps beat fewer instructions per element).
+// One PRMT builds
 // the shared-memory address of a code byte's entry in a 64 KB table of float
 // pairs (16 replicas x 256 byte values x 2 tables, replica = lane % 16, so a
 // warp lookup touches every bank exactly twice) and one 64-bit load returns
@@ -62,7 +65,7 @@ namespace {
 typedef unsigned long long u64;
 
 #ifndef LATENT_DECODE_WARPS
-#define LATENT_DECODE_WARPS 12
+#define LATENT_DECODE_WARPS 16
 #endif
 constexpr int kSW = LATENT_DECODE_WARPS;                 // warps per CTA
 constexpr int kSThreads = kSW * 32;
@@ -173,7 +176,7 @@ __device__ bool wait_ge(const uint32_t *flag, uint32_t target, uint32_t *err) {
         }
         // long sleeps: a polling warp takes issue slots from the warps still computing
         __nanosleep(ns);
-        if (ns < 2048) ns <<= 1;
+        if (ns < 512) ns <<= 1;
     }
 }
 
@@ -431,9 +434,12 @@ __device__ __forceinline__ void issue_stage(const DecodeArgs &a, Issuer &is, uin
 }
 
 // ---------------------------------------------------------------------------
+#ifndef LATENT_DECODE_COLS
+#define LATENT_DECODE_COLS 8
+#endif
 template <int NT>
 struct Mode {
-    static constexpr int COLS = NT <= 4 ? 16 : 8;  // columns per lane
+    static constexpr int COLS = NT <= 4 ? LATENT_DECODE_COLS : 8;  // columns per lane
     static constexpr int NB = COLS / 2;            // code bytes per lane and row
 };
 
