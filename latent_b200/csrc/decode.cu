@@ -95,7 +95,8 @@ static_assert(kWarpBytes % 16 == 0, "warp area alignment");
 // CTA area at the start of dynamic shared memory, then the areas of the low
 // warps, the pair table at shared address 64 K, the remaining warps after it.
 constexpr int kCumCap = 1024;          // virtual experts whose cost prefix is kept in shared memory
-constexpr int kCtaBytes = 512 + (kCumCap + 4) * 4;
+constexpr int kCtaRange = 512 + (kCumCap + 4) * 4;     // Pos [4][kSW + 1] phase ranges of the CTA's warps
+constexpr int kCtaBytes = kCtaRange + ((4 * (kSW + 1) * 12 + 15) / 16) * 16;
 constexpr uint32_t kTableAddr = 65536;
 constexpr int kTableBytes = 65536;
 constexpr int kMaxSmemBase = 4096;      // dynamic shared memory must start below this address
@@ -199,9 +200,11 @@ struct Geo {
 
 // Cost-weight prefix of virtual expert v (cum(n_virt) = total weight), from
 // shared memory when it fits there, else from the virtual-expert table.
+struct Pos;
 struct CumView {
     const int *s;      // [n + 1] or nullptr
     const int4 *virt;
+    const Pos *rng;    // phase ranges of the CTA's warps (see iter_next)
     int n, total;
     __device__ __forceinline__ int operator()(int v) const {
         if (s) return s[v];
@@ -313,8 +316,9 @@ struct Iter {
 };
 static_assert(sizeof(Iter) <= 48, "iterator area");
 
-// Moves to the next non-empty piece; false when all phases are done.
-__device__ bool iter_next(Iter &it, const Geo *geo, int gw, const CumView &cum) {
+// Moves to the next non-empty piece; false when all phases are done.  rng
+// holds range_start of phase P for the CTA's warps 0..kSW at rng[(P-1)*(kSW+1) + w].
+__device__ bool iter_next(Iter &it, const Geo *geo, int gw, const Pos *rng) {
     while (true) {
         if (it.P >= 1 && it.P <= 4 && pos_less(it.cur, it.end)) {
             const Geo &g = geo[it.P - 1];
@@ -337,8 +341,9 @@ __device__ bool iter_next(Iter &it, const Geo *geo, int gw, const CumView &cum) 
         ++it.P;
         const Geo &g = geo[it.P - 1];
         if (gw < g.Gp) {
-            it.cur = range_start(g, gw, cum);
-            it.end = range_start(g, gw + 1, cum);
+            const Pos *r = rng + (it.P - 1) * (kSW + 1) + (gw % kSW);
+            it.cur = r[0];
+            it.end = r[1];
         } else {
             it.cur = it.end = Pos{0, 0, 0};
         }
@@ -353,7 +358,7 @@ __device__ __forceinline__ const latent_qmatrix &phase_matrix(const DecodeArgs &
 __device__ __forceinline__ bool shared_iter_next(Iter *itp, Iter &it, const Geo *geo, int gw, const CumView &cum,
                                                  int lane) {
     it = *itp;
-    const bool more = iter_next(it, geo, gw, cum);
+    const bool more = iter_next(it, geo, gw, cum.rng);
     __syncwarp();
     if (lane == 0) *itp = it;
     __syncwarp();
@@ -963,6 +968,20 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
     }
     __syncthreads();
     if (threadIdx.x == 0) atomicAdd(args.zero_done, 1u);
+    CumView cv;
+    cv.s = nv <= kCumCap ? cta_cum : nullptr;
+    cv.virt = args.rt.virt;
+    cv.n = nv;
+    cv.total = wtot;
+    // the ranges of every phase for this CTA's warps, once (range_start of
+    // warps blockIdx.x * kSW + 0 .. kSW, clamped to the phase's warp count)
+    Pos *cta_rng = reinterpret_cast<Pos *>(dsm + kCtaRange);
+    cv.rng = cta_rng;
+    for (int t = threadIdx.x; t < 4 * (kSW + 1); t += kSThreads) {
+        const int P = t / (kSW + 1), w = blockIdx.x * kSW + (t - P * (kSW + 1));
+        cta_rng[t] = range_start(geo[P], w < geo[P].Gp ? w : geo[P].Gp, cv);
+    }
+    __syncthreads();
     WarpCtx wc;
     wc.geo = geo;
     wc.warea = warea;
@@ -971,10 +990,7 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
     wc.lb = (kTableAddr & 0xFFFF0000u) | (uint32_t)((lane & 15) * 8);
     wc.gw = gw;
     wc.lane = lane;
-    wc.cum.s = nv <= kCumCap ? cta_cum : nullptr;
-    wc.cum.virt = args.rt.virt;
-    wc.cum.n = nv;
-    wc.cum.total = wtot;
+    wc.cum = cv;
     Iter *cit = reinterpret_cast<Iter *>(warea + kWIter);
     if (lane == 0) {
         Iter z;
