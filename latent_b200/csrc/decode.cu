@@ -19,9 +19,9 @@
 // synchronisation).  A warp's range covers parts ("pieces") of one or a few
 // segments.  A piece accumulates its rows in registers and adds the sums of
 // its columns into the phase output with vector atomic adds (the outputs are
-// zeroed at kernel start, before any piece adds), then counts itself in on
+// zeroed at kernel start, before any piece adds), then adds its row count to
 // the segment's arrival counter.  A piece of the next phase waits (bounded)
-// until every piece of the segments it reads has arrived; the SwiGLU (and
+// until all rows of the segments it reads have arrived; the SwiGLU (and
 // the optional router weight) is applied where phase 3 loads its inputs.
 // Every CTA is resident (cooperative launch) and every warp takes its ranges
 // in phase order, so every wait ends; a wait that exceeds its bound sets
@@ -215,11 +215,6 @@ struct CumView {
 __device__ __forceinline__ int tile_w(const Geo &g, int c) { return c == g.C - 1 ? g.wl : 256; }
 __device__ __forceinline__ int seg_m(const Geo &g, int j) { return g.P == 2 ? (j & 1) : j / g.C; }
 __device__ __forceinline__ int seg_c(const Geo &g, int j) { return g.P == 2 ? (j >> 1) : j % g.C; }
-__device__ __forceinline__ int64_t seg_off(const Geo &g, int j) {
-    const int m = seg_m(g, j), c = seg_c(g, j);
-    if (g.P == 2) return (int64_t)c * 2 * g.Uf + (int64_t)m * (c == g.C - 1 ? g.Ul : g.Uf);
-    return (int64_t)m * g.Wm + (int64_t)c * g.Uf;
-}
 
 __device__ Geo make_geo(const DecodeArgs &a, int P, int n_virt, int wtot, int G) {
     Geo g;
@@ -291,17 +286,6 @@ __device__ Pos range_start(const Geo &g, int w, const CumView &cum) {
 
 __device__ __forceinline__ bool pos_less(const Pos &a, const Pos &b) {
     return a.v != b.v ? a.v < b.v : a.j != b.j ? a.j < b.j : a.blk < b.blk;
-}
-
-// The warp owning block blk of segment (v, j): the last w with start(w) <= block.
-__device__ int owner(const Geo &g, int v, int j, int blk, const CumView &cum) {
-    const int wb = tile_w(g, seg_c(g, j)) / 32;
-    const int c0 = cum(v), wt = cum(v + 1) - c0;
-    const int64_t end = (int64_t)c0 * g.Wv + (int64_t)wt * (seg_off(g, j) + (int64_t)(blk + 1) * wb);
-    int w = (int)((end * g.Gp + g.total - 1) / g.total) - 1;
-    if (w < 0) w = 0;
-    if (w > g.Gp - 1) w = g.Gp - 1;
-    return w;
 }
 
 // ---------------------------------------------------------------------------
@@ -718,32 +702,12 @@ __device__ __forceinline__ int flag_index(const Geo &g, int v, int j) {
     return g.P == 2 ? v * g.C + (j >> 1) : v * g.S + j;
 }
 
-// Pieces of segment (v, j) of phase P: the warps first..last; for phase 2
-// the gate and up segments of a tile form one reduction group.
-struct SegPieces {
-    int j0, nj;          // first segment of the group, segments in it (1 or 2)
-    int first[2], q[2];  // first piece warp and piece count of each segment
-    int total;           // pieces of the group
-};
-
-__device__ __forceinline__ SegPieces seg_pieces(const Geo &g, int v, int j, const CumView &cum) {
-    SegPieces sp;
-    sp.j0 = g.P == 2 ? (j & ~1) : j;
-    sp.nj = g.P == 2 ? 2 : 1;
-    sp.total = 0;
-    for (int q = 0; q < sp.nj; ++q) {
-        sp.first[q] = owner(g, v, sp.j0 + q, 0, cum);
-        sp.q[q] = owner(g, v, sp.j0 + q, g.L / 8 - 1, cum) - sp.first[q] + 1;
-        sp.total += sp.q[q];
-    }
-    return sp;
-}
-
 // Piece end: the lane-row reduction, the vector atomic adds into the phase
 // output (after the kernel-start zeroing is complete), the arrival count.
 template <int NT>
-__device__ __forceinline__ void flush_piece(const DecodeArgs &a, const Geo &g, int v, int j, int p0, int nt, int lane,
-                                            int rs, int ch, int lpr, bool active, bool &zeroed, u64 (&acc)[32]) {
+__device__ __forceinline__ void flush_piece(const DecodeArgs &a, const Geo &g, int v, int j, int p0, int nt, int rows,
+                                            int lane, int rs, int ch, int lpr, bool active, bool &zeroed,
+                                            u64 (&acc)[32]) {
     constexpr int NB = Mode<NT>::NB, COLS = Mode<NT>::COLS;
     for (int o = lpr; o < 32; o <<= 1) {
 #pragma unroll
@@ -788,26 +752,24 @@ __device__ __forceinline__ void flush_piece(const DecodeArgs &a, const Geo &g, i
     for (int i = 0; i < 32; ++i) acc[i] = 0ull;
     __threadfence();
     __syncwarp();
-    if (lane == 0) atomicAdd(a.arrive[g.P - 1] + flag_index(g, v, j), 1u);
+    if (lane == 0) atomicAdd(a.arrive[g.P - 1] + flag_index(g, v, j), (uint32_t)rows);
 }
 
-// Bounded wait (lane 0) until every piece of segment (v, j) of phase g.P
-// (phase 2: of the gate/up pair) has arrived.
-__device__ __forceinline__ bool wait_segment(const DecodeArgs &a, const Geo &g, int v, int j, const CumView &cum) {
-    const SegPieces sp = seg_pieces(g, v, j, cum);
-    return wait_ge(a.arrive[g.P - 1] + flag_index(g, v, j), (uint32_t)sp.total, a.rt.err);
+// Bounded wait (lane 0) until every row of segment (v, j) of phase g.P
+// (phase 2: of the gate/up pair) has arrived: pieces count their rows in.
+__device__ __forceinline__ bool wait_segment(const DecodeArgs &a, const Geo &g, int v, int j) {
+    return wait_ge(a.arrive[g.P - 1] + flag_index(g, v, j), (uint32_t)(g.P == 2 ? 2 * g.L : g.L), a.rt.err);
 }
 
 // Bounded wait (lane 0) for the previous-phase segments holding input rows
 // [row0, row1) of a piece of phase P: phase 2 reads t_m (phase-1 segment
 // (m, c)), phase 3 reads h (phase-2 pair c), phase 4 reads s (phase-3 segment c).
-__device__ void wait_inputs(const DecodeArgs &a, const Geo *geo, int P, int v, int m, int row0, int row1,
-                            const CumView &cum, int lane) {
+__device__ void wait_inputs(const DecodeArgs &a, const Geo *geo, int P, int v, int m, int row0, int row1, int lane) {
     if (P == 1 || lane != 0) return;
     const Geo &gp = geo[P - 2];
     for (int c = row0 / 256; c <= (row1 - 1) / 256; ++c) {
         const int j = P == 2 ? m * gp.C + c : P == 3 ? 2 * c : c;
-        if (!wait_segment(a, gp, v, j, cum)) return;
+        if (!wait_segment(a, gp, v, j)) return;
     }
 }
 
@@ -856,7 +818,7 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
         for (int k = 0; k < 4; ++k)
             if (4 * tq + k < nt) pw[k] = load_weight(a.weights, a.w_type, a.rt.order[p0 + 4 * tq + k]);
     }
-    wait_inputs(a, wc.geo, P, v, m, it.row, row1, wc.cum, lane);
+    wait_inputs(a, wc.geo, P, v, m, it.row, row1, lane);
     __syncwarp();
     uint32_t pre[4];
     float preu[4];
@@ -916,7 +878,7 @@ __device__ __forceinline__ void run_piece(const DecodeArgs &a, const WarpCtx &wc
         __syncwarp();
         row += n;
     }
-    flush_piece<NT>(a, g, v, j, p0, nt, lane, rs, ch, lpr, active, zeroed, acc);
+    flush_piece<NT>(a, g, v, j, p0, nt, row1 - it.row, lane, rs, ch, lpr, active, zeroed, acc);
 }
 
 // ---------------------------------------------------------------------------
@@ -1036,7 +998,7 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
             const int p = a.rt.pos[row];
             float4 y0 = make_float4(0.f, 0.f, 0.f, 0.f), y1 = y0;
             if (p >= 0) {
-                if (lane == 0) wait_segment(a, g4, a.rt.vslot[p], c, wc.cum);
+                if (lane == 0) wait_segment(a, g4, a.rt.vslot[p], c);
                 __syncwarp();
                 if (live_col) {
                     const float4 *y = reinterpret_cast<const float4 *>(a.y + (int64_t)p * a.d + col);
@@ -1056,7 +1018,7 @@ __global__ void __launch_bounds__(kSThreads, 1) k_decode(DecodeArgs args) {
             const int slot = row * a.k + jj;
             const int p = a.rt.pos[slot];
             if (p < 0) continue;
-            if (lane == 0) wait_segment(a, g4, a.rt.vslot[p], c, wc.cum);
+            if (lane == 0) wait_segment(a, g4, a.rt.vslot[p], c);
             __syncwarp();
             const float wt = wbd ? 1.f : load_weight(a.weights, a.w_type, slot);
             if (live_col) {
