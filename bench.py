@@ -61,6 +61,10 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bound on the CPU baseline's timed work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill leg of the default run")
+    ap.add_argument("--ep-exact", action="store_true",
+                    help="expert parallel: exact splits with a host read of the counts (default: fixed capacity)")
+    ap.add_argument("--ep-graph", action="store_true",
+                    help="expert parallel: replay the fixed-capacity step as one captured CUDA graph")
     return ap.parse_args()
 
 
@@ -339,6 +343,8 @@ def run_ours(args, world, rank, local):
         "clocks": clk,
         "gen_s": gen_s,
     }
+    if world == 1:
+        line["router"] = run_router(dev, flush, steps=max(args.steps, 5), warmup=max(args.warmup, 3))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_leg(cfg, es, x, ids, w, args.cpu_seconds)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -347,6 +353,29 @@ def run_ours(args, world, rank, local):
         torch.cuda.empty_cache()
         line["prefill"] = run_prefill(args, 2, dev, steps=max(5, min(args.steps, 20)), warmup=args.warmup)
     return line
+
+
+def run_router(dev, flush, steps: int, warmup: int, T: int = 16384, E: int = 256, k: int = 8):
+    """Adaptive top-k router (latent_router_topk) on config 3's routing shape, L2 flushed before each call."""
+    from latent_b200 import router_topk
+    g = torch.Generator(device=dev).manual_seed(3)
+    scores = torch.softmax(torch.randn((T, E), generator=g, device=dev), dim=1)
+    for _ in range(warmup):
+        router_topk(scores, k)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev:
+        flush()
+        a.record()
+        ids, w, nk = router_topk(scores, k)
+        b.record()
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    nbytes = T * E * 4 + T * k * 8 + T * 4
+    pk = peaks()
+    return {"shape": {"tokens": T, "experts": E, "top_k": k, "threshold": 0.95}, "ms": ms,
+            "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (ms * 1e-3) / 1e9,
+            "frac_hbm": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+            "mean_kept": float(nk.float().mean())}
 
 
 PREFILL_PHASES = ["route", "dequant+gather", "G1 x.[A_g|A_u]", "G2 silu(t_g.B_g)*(t_u.B_u)", "G3 h.A_d",
@@ -435,11 +464,28 @@ def run_ours_ep(args, world, rank, local):
     x, ids, w = synth.make_batch(cfg, dev, seed_offset=rank)
     gen_s = time.perf_counter() - t0
     ops = _TimedOps(CudaEPOps(es, cfg.n_expert))
-    ep = ExpertParallelFFN(cfg.n_expert, ops)
+    ep = ExpertParallelFFN(cfg.n_expert, ops, max_tokens=None if args.ep_exact else x.shape[0])
     flush = L2Flush(dev)
     for _ in range(max(args.warmup, 3)):
         ep(x, ids, w)
     torch.cuda.synchronize()
+    step = lambda: ep(x, ids, w)
+    graph = None
+    if args.ep_graph and not args.ep_exact:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                ep(x, ids, w)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        barrier(world)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ep(x, ids, w)
+        torch.cuda.synchronize()
+        barrier(world)
+        step = graph.replay
     steps = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     ffn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     recv_rows = []
@@ -449,16 +495,24 @@ def run_ours_ep(args, world, rank, local):
     clocks.start()
     for k in range(args.steps):
         flush()
-        ops.ev = ffn[k]
+        ops.ev = None if graph is not None else ffn[k]
         steps[k][0].record()
-        ep(x, ids, w)
+        step()
         steps[k][1].record()
-        recv_rows.append(sum(ep.last_counts[1]))
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     clk = clocks.stop()
     ops.ev = None
+    if graph is not None:
+        # the local FFN alone, eagerly, for the roofline numerator's time
+        for k in range(args.steps):
+            flush()
+            ops.ev = ffn[k]
+            ep(x, ids, w)
+        torch.cuda.synchronize()
+        ops.ev = None
+    recv_rows.append(sum(ep.last_counts[1]))
     ms_local = statistics.mean(a.elapsed_time(b) for a, b in steps)
     ffn_ms = statistics.mean(a.elapsed_time(b) for a, b in ffn)
     ms = allreduce_max(ms_local, world)
@@ -473,6 +527,13 @@ def run_ours_ep(args, world, rank, local):
     hout = torch.empty((x.shape[0], cfg.n_embd), dtype=torch.float32).pin_memory()
     dx, dids, dw = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(w)
     e2e = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    e2e_graph = None
+    if graph is not None:
+        e2e_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(e2e_graph):
+            e2e_out = ep(dx, dids, dw)
+        torch.cuda.synchronize()
+        barrier(world)
     for k in range(args.warmup + args.steps):
         flush()
         if k >= args.warmup:
@@ -480,18 +541,25 @@ def run_ours_ep(args, world, rank, local):
         dx.copy_(hx, non_blocking=True)
         dids.copy_(hids, non_blocking=True)
         dw.copy_(hw, non_blocking=True)
-        out = ep(dx, dids, dw)
+        if e2e_graph is not None:
+            e2e_graph.replay()
+            out = e2e_out
+        else:
+            out = ep(dx, dids, dw)
         hout.copy_(out, non_blocking=True)
         if k >= args.warmup:
             e2e[k - args.warmup][1].record()
     torch.cuda.synchronize()
     e2e_ms = allreduce_max(statistics.mean(a.elapsed_time(b) for a, b in e2e), world)
+    del graph, e2e_graph   # graphs holding NCCL work are released before the process group
     R = ids.numel()
     return {
         "metric": METRIC, "value": routed_all / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE recipe)",
-        "config": config_json(cfg, ids, world, f"expert-parallel ep{world} (NCCL all-to-all)"),
+        "config": config_json(cfg, ids, world, f"expert-parallel ep{world} (NCCL all-to-all, "
+                              f"{'exact splits' if args.ep_exact else 'fixed capacity'}"
+                              f"{', CUDA graph' if args.ep_graph and not args.ep_exact else ''})"),
         "roofline": {"bound": "hbm", "kernel": "local fused expert FFN (rank 0)", "achieved": ach,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "traffic": None,
                      "algorithmic_bytes": local_bytes, "mean_ms": ffn_ms, "peak_source": pk["source"]},

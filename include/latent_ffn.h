@@ -239,6 +239,28 @@ LATENT_API int latent_silu(const float *x, float *y, int64_t n, struct CUstream_
 LATENT_API int latent_pack_tiles(const uint8_t *codes, const uint16_t *scales, int32_t n_expert, int64_t rows,
                                  int64_t cols, uint8_t *dst_codes, uint16_t *dst_scales, struct CUstream_st *stream);
 
+/* Adaptive top-k router (reference loader/adaptive_topk.py:29-90,
+ * adaptive_topk_inclusive / adaptive_topk_batch).  scores[n_tokens][n_expert]
+ * fp32 router scores (e.g. softmax probabilities) -> per token its top_k
+ * experts in descending score order (ties: lower expert id first), of which
+ * the leading ones are kept while their float32 running sum stays within
+ * threshold x the float32 sum of the top_k (compared in float32, as numpy 2
+ * evaluates the reference).  ids[n_tokens][top_k] int32: kept expert ids,
+ * -1 for dropped slots (the fused op skips them).  weights[n_tokens][top_k]
+ * fp32: kept scores divided by their float32 sum with
+ * LATENT_ROUTER_RENORMALIZE, else the raw scores; 0 for dropped slots.
+ * n_kept[n_tokens] (optional, may be NULL): kept slots per token.  A token
+ * whose top_k sum is <= 0 keeps none.  Errors: LATENT_ERR_SHAPE for
+ * top_k < 1 or top_k > n_expert (the reference raises ValueError),
+ * LATENT_ERR_INVALID for threshold outside (0, 1] (ValueError there) or
+ * unknown flags, LATENT_ERR_UNSUPPORTED beyond 1024 experts or top_k 32.
+ * Scores are expected finite; a NaN score is never selected.  Stream-ordered,
+ * allocates nothing; ids/weights feed latent_expert_ffn_forward directly. */
+enum { LATENT_ROUTER_RENORMALIZE = 1u << 0 };
+LATENT_API int latent_router_topk(const float *scores, int32_t n_tokens, int32_t n_expert, int32_t top_k,
+                                  double threshold, uint32_t flags, int32_t *ids, float *weights, int32_t *n_kept,
+                                  struct CUstream_st *stream);
+
 #ifdef __cplusplus
 }
 #endif

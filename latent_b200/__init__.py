@@ -9,10 +9,10 @@ the batched routed op:
 from .format import ExpertSet, GroupedFactor, StackedFactor, from_int8, from_mixed, from_nf4, from_npz
 from .quant import quantize_factor
 from .runtime import (ExpertFFN, FactorPair, dense_swiglu_expert, dequantize, load_pair, moe_expert_ffn,
-                      project, silu, swiglu_expert, workspace_bytes)
+                      project, router_topk, silu, swiglu_expert, workspace_bytes)
 
 __all__ = [
     "ExpertSet", "GroupedFactor", "StackedFactor", "from_int8", "from_mixed", "from_nf4", "from_npz",
     "quantize_factor", "ExpertFFN", "FactorPair", "dense_swiglu_expert", "dequantize", "load_pair",
-    "moe_expert_ffn", "project", "silu", "swiglu_expert", "workspace_bytes",
+    "moe_expert_ffn", "project", "router_topk", "silu", "swiglu_expert", "workspace_bytes",
 ]

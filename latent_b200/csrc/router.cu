@@ -1,0 +1,163 @@
+// Adaptive top-k router: router scores -> (expert ids, combine weights) for
+// the fused op.  Reference: loader/adaptive_topk.py:29-90
+// (adaptive_topk_inclusive / adaptive_topk_batch), which keeps, of a token's
+// top-k scores in descending order, the leading ones whose running sum stays
+// within threshold x their total.  Dropped slots get id -1, which the fused op
+// skips (kernels/latent_fused_expert_ffn.cu:33-40 treats id < 0 as a zero row).
+//
+// One warp per token.  Lane l holds scores l, l+32, ... of the row in
+// registers (coalesced 128-byte loads); k rounds of a warp arg-max (larger
+// score first, lower expert id on ties) produce the descending top-k, which
+// lane 0 then scans with the reference's arithmetic: the total is numpy's
+// float32 pairwise sum, the target threshold x total is formed in double and
+// compared in float32, the running sum is float32.  HBM-bound: one read of the
+// scores, k ids + k weights written per token.
+#include "internal.h"
+
+namespace latent {
+
+namespace {
+
+constexpr int kRouterWarps = 8;
+constexpr int kMaxRouterTopK = 32;       // one arg-max round per slot
+constexpr int kMaxRouterExperts = 1024;  // 32 scores per lane in registers
+
+bool router_aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+// np.sum of n <= 32 float32 values: sequential from zero below 8 values, else
+// eight strided accumulators combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7))
+// and then the tail (numpy's pairwise summation for short vectors).
+__device__ float f32_sum(const float *a, int n) {
+    if (n < 8) {
+        float r = 0.f;
+        for (int i = 0; i < n; ++i) r = __fadd_rn(r, a[i]);
+        return r;
+    }
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = a[j];
+    int i = 8;
+    for (; i < n - n % 8; i += 8)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], a[i + j]);
+    float r = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3])),
+                        __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7])));
+    for (; i < n; ++i) r = __fadd_rn(r, a[i]);
+    return r;
+}
+
+template <int NPL>
+__global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(const float *__restrict__ scores, int T, int E,
+                                                                    int k, double threshold, bool renorm,
+                                                                    int *__restrict__ ids, float *__restrict__ weights,
+                                                                    int *__restrict__ n_kept) {
+    __shared__ float s_val[kRouterWarps][kMaxRouterTopK];
+    __shared__ int s_idx[kRouterWarps][kMaxRouterTopK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * kRouterWarps + warp;
+    if (t >= T) return;
+    const float *row = scores + (size_t)t * E;
+    float v[NPL];
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+        const int e = j * 32 + lane;
+        v[j] = e < E ? __ldg(row + e) : -INFINITY;
+    }
+    unsigned taken = 0;
+    for (int r = 0; r < k; ++r) {
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) {
+            const int e = j * 32 + lane;
+            const bool better = v[j] > bv || (v[j] == bv && e < bi);   // NaN never wins
+            if (e < E && !((taken >> j) & 1u) && better) {
+                bv = v[j];
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bi < E && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+        if (lane == 0) {
+            s_val[warp][r] = bi < E ? bv : 0.f;
+            s_idx[warp][r] = bi < E ? bi : -1;
+        }
+    }
+    __syncwarp();
+    if (lane != 0) return;
+    const float *sv = s_val[warp];
+    const int *si = s_idx[warp];
+    // adaptive_topk_inclusive (loader/adaptive_topk.py:46-56)
+    const float total = f32_sum(sv, k);
+    int n = k;
+    float cum = 0.f;
+    if (total <= 0.f) {
+        n = 0;
+    } else {
+        const float target = __double2float_rn(threshold * (double)total);
+        for (int i = 0; i < k; ++i) {
+            const float next = __fadd_rn(cum, sv[i]);
+            if (next > target) {
+                n = i;
+                break;
+            }
+            cum = next;
+        }
+    }
+    for (int i = 0; i < k; ++i) {
+        const bool keep = i < n && si[i] >= 0;
+        ids[(size_t)t * k + i] = keep ? si[i] : -1;
+        weights[(size_t)t * k + i] = keep ? (renorm ? __fdiv_rn(sv[i], cum) : sv[i]) : 0.f;
+    }
+    if (n_kept) n_kept[t] = n;
+}
+
+template <int NPL>
+void launch(const float *scores, int T, int E, int k, double threshold, bool renorm, int *ids, float *w, int *nk,
+            cudaStream_t s) {
+    const int blocks = (T + kRouterWarps - 1) / kRouterWarps;
+    k_router_topk<NPL><<<blocks, kRouterWarps * 32, 0, s>>>(scores, T, E, k, threshold, renorm, ids, w, nk);
+}
+
+}  // namespace
+
+cudaError_t launch_router_topk(const float *scores, int T, int E, int k, double threshold, bool renorm, int *ids,
+                               float *weights, int *n_kept, cudaStream_t s) {
+    if (T == 0) return cudaSuccess;
+    if (E <= 32) launch<1>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
+    else if (E <= 64) launch<2>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
+    else if (E <= 128) launch<4>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
+    else if (E <= 256) launch<8>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
+    else if (E <= 512) launch<16>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
+    else launch<32>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
+    return cudaGetLastError();
+}
+
+}  // namespace latent
+
+extern "C" LATENT_API int latent_router_topk(const float *scores, int32_t n_tokens, int32_t n_expert, int32_t top_k,
+                                             double threshold, uint32_t flags, int32_t *ids, float *weights,
+                                             int32_t *n_kept, CUstream_st *stream) {
+    using namespace latent;
+    if (n_tokens < 0 || n_expert < 1 || top_k < 1 || top_k > n_expert) return LATENT_ERR_SHAPE;
+    if (!(threshold > 0.0 && threshold <= 1.0)) return LATENT_ERR_INVALID;
+    if (flags & ~(uint32_t)LATENT_ROUTER_RENORMALIZE) return LATENT_ERR_INVALID;
+    if (n_expert > kMaxRouterExperts || top_k > kMaxRouterTopK) return LATENT_ERR_UNSUPPORTED;
+    if (n_tokens == 0) return LATENT_OK;
+    if (!scores || !ids || !weights) return LATENT_ERR_INVALID;
+    if (!router_aligned(scores, 4) || !router_aligned(ids, 4) || !router_aligned(weights, 4) ||
+        (n_kept && !router_aligned(n_kept, 4)))
+        return LATENT_ERR_ALIGN;
+    const cudaError_t e = launch_router_topk(scores, n_tokens, n_expert, top_k, threshold,
+                                             (flags & LATENT_ROUTER_RENORMALIZE) != 0, ids, weights, n_kept,
+                                             reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? LATENT_OK : LATENT_ERR_CUDA;
+}

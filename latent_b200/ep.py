@@ -4,7 +4,9 @@ Experts are contiguous per rank (rank g owns experts [g*E/G, (g+1)*E/G)).
 One call, on every rank:
   1. dispatch (CUDA library): route the local batch by global expert id and
      pack one row per routed slot in expert order = destination-rank order;
-  2. all-to-all of per-destination row counts, one host read of the counts;
+  2. all-to-all of per-destination row counts, one host read of the counts
+     (or, with a fixed token capacity, no count exchange: fixed-size blocks
+     per destination whose unused rows carry expert id -1);
   3. all-to-all of the rows (x in its dtype) and of (expert id, weight);
   4. the fused latent FFN over the received rows with the local experts
      (top-1, weight 1 -- or the router weight before the down projection);
@@ -93,22 +95,52 @@ class CudaEPOps:
 
 
 class ExpertParallelFFN:
-    """Routed expert FFN with experts sharded over the ranks of ``group``."""
+    """Routed expert FFN with experts sharded over the ranks of ``group``.
 
-    def __init__(self, n_expert: int, ops, group=None):
+    Two exchange modes:
+      * ``max_tokens=None``: exact splits.  Per-destination row counts are
+        exchanged first and read on the host to size the row all-to-alls.
+      * ``max_tokens=M`` (M = the most tokens any rank passes in one call, the
+        same on every rank): fixed-capacity splits, no host read.  Each rank
+        sends every destination a block of ``cap = M * min(k, E/G)`` rows
+        (a token routes at most that many slots to one rank); rows past a
+        destination's count carry expert id -1, which the fused op skips.
+        The whole call is stream-ordered, so consecutive calls pipeline and
+        the call can be captured with its collectives.
+    """
+
+    def __init__(self, n_expert: int, ops, group=None, max_tokens: Optional[int] = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if n_expert % self.world:
             raise ValueError(f"{n_expert} experts do not split evenly over {self.world} ranks")
+        if max_tokens is not None and max_tokens < 1:
+            raise ValueError(f"max_tokens must be positive, got {max_tokens}")
         self.n_expert = n_expert
         self.e_local = n_expert // self.world
         self.base = self.rank * self.e_local
         self.ops = ops
-        self.last_counts = None
+        self.max_tokens = max_tokens
+        self._counts = None
+        self._pos = None
+
+    @property
+    def last_counts(self):
+        """(rows sent to each rank, rows received from each rank) of the last call, as lists."""
+        if self._counts is None:
+            return None
+        sc, rc = self._counts
+        if torch.is_tensor(sc):
+            both = torch.stack([sc.to(torch.int64), rc.to(torch.int64)]).cpu()
+            sc, rc = both[0].tolist(), both[1].tolist()
+            self._counts = (sc, rc)
+        return sc, rc
 
     def __call__(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
                  weight_before_down: bool = False) -> torch.Tensor:
+        if self.max_tokens is not None:
+            return self._call_fixed(x, ids, weights, weight_before_down)
         G, d = self.world, x.shape[1]
         p = self.ops.dispatch(x, ids, weights, weight_before_down)
         send_counts = p.expert_counts.view(G, self.e_local).sum(dim=1).to(torch.int64)
@@ -116,7 +148,7 @@ class ExpertParallelFFN:
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         both = torch.stack([send_counts, recv_counts]).cpu()
         sc, rc = both[0].tolist(), both[1].tolist()
-        self.last_counts = (sc, rc)
+        self._counts = (sc, rc)
         n_send, n_recv = sum(sc), sum(rc)
         recv_x = torch.empty((n_recv, d), dtype=x.dtype, device=x.device)
         dist.all_to_all_single(recv_x, p.send_x[:n_send].contiguous(), rc, sc, group=self.group)
@@ -131,4 +163,44 @@ class ExpertParallelFFN:
         y = self.ops.local_ffn(recv_x, local_ids, rw, weight_before_down)
         y_back = torch.empty((max(n_send, 1), d), dtype=torch.float32, device=x.device)
         dist.all_to_all_single(y_back[:n_send], y.contiguous(), sc, rc, group=self.group)
+        return self.ops.combine(p, y_back)
+
+    def _call_fixed(self, x, ids, weights, wbd):
+        G, d = self.world, x.shape[1]
+        T, k = ids.shape
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens}")
+        cap = self.max_tokens * min(k, self.e_local)
+        dev = x.device
+        p = self.ops.dispatch(x, ids, weights, wbd)
+        P = p.send_x.shape[0]
+        send_counts = p.expert_counts.view(G, self.e_local).sum(dim=1).to(torch.int64)
+        end = torch.cumsum(send_counts, 0)
+        if self._pos is None or self._pos.numel() < P or self._pos.device != dev:
+            self._pos = torch.arange(max(P, 1), dtype=torch.int64, device=dev)
+        pos = self._pos[:P]
+        g = torch.searchsorted(end, pos, right=True)             # destination rank; G past the routed rows
+        gc = g.clamp(max=G - 1)
+        slot = pos - (end - send_counts)[gc]
+        dst = torch.where(g < G, gc * cap + slot, torch.full_like(pos, G * cap))   # row G*cap: discard
+        send_x = torch.empty((G * cap + 1, d), dtype=x.dtype, device=dev)
+        send_x.index_copy_(0, dst, p.send_x)
+        meta = torch.stack([p.send_expert[:P], p.send_weight[:P].view(torch.int32)], dim=1)
+        send_meta = torch.full((G * cap + 1, 2), -1, dtype=torch.int32, device=dev)
+        send_meta.index_copy_(0, dst, meta)
+        recv_x = torch.empty((G * cap, d), dtype=x.dtype, device=dev)
+        dist.all_to_all_single(recv_x, send_x[:G * cap], group=self.group)
+        recv_meta = torch.empty((G * cap, 2), dtype=torch.int32, device=dev)
+        dist.all_to_all_single(recv_meta, send_meta[:G * cap], group=self.group)
+        rid = recv_meta[:, 0]
+        local_ids = torch.where(rid >= 0, rid - self.base, rid).reshape(-1, 1).contiguous()
+        if wbd:
+            rw = recv_meta[:, 1].contiguous().view(torch.float32).reshape(-1, 1).contiguous()
+        else:
+            rw = torch.ones((G * cap, 1), dtype=torch.float32, device=dev)
+        y = self.ops.local_ffn(recv_x, local_ids, rw, wbd)
+        y_pad = torch.empty((G * cap, d), dtype=torch.float32, device=dev)
+        dist.all_to_all_single(y_pad, y.contiguous(), group=self.group)
+        y_back = y_pad.index_select(0, dst.clamp(max=G * cap - 1))
+        self._counts = (send_counts, (rid.view(G, cap) >= 0).sum(dim=1))
         return self.ops.combine(p, y_back)

@@ -23,7 +23,7 @@ from . import _lib
 from .format import ExpertSet, GroupedFactor, from_npz
 
 __all__ = ["FactorPair", "load_pair", "project", "silu", "swiglu_expert", "dense_swiglu_expert",
-           "moe_expert_ffn", "ExpertFFN", "workspace_bytes", "dequantize"]
+           "moe_expert_ffn", "ExpertFFN", "workspace_bytes", "dequantize", "router_topk"]
 
 _X_TYPES = {torch.float32: _lib.TYPE_F32, torch.float16: _lib.TYPE_F16, torch.bfloat16: _lib.TYPE_BF16}
 _W_TYPES = {torch.float32: _lib.TYPE_F32, torch.float16: _lib.TYPE_F16}
@@ -259,6 +259,39 @@ def _to_dev(a, dev, dtype=None):
 
 
 _OPS: Dict[int, ExpertFFN] = {}
+
+
+def router_topk(scores: torch.Tensor, top_k: int, threshold: float = 0.95, renormalize: bool = True):
+    """Adaptive top-k routing on the device (latent_router_topk).
+
+    scores: [T, E] fp32 router scores on a CUDA device.  Returns (ids [T, k]
+    int32, weights [T, k] fp32, n_kept [T] int32): the top-k experts in
+    descending score order, the tail beyond the reference's inclusive
+    threshold rule dropped to id -1 / weight 0 (loader/adaptive_topk.py:29-90),
+    kept weights renormalised to sum to 1 unless ``renormalize`` is False.
+    The ids and weights feed ``ExpertFFN`` / ``moe_expert_ffn`` directly.
+    Raises ValueError where the reference does (threshold outside (0, 1],
+    top_k > n_experts, scores not 2-D)."""
+    if not torch.is_tensor(scores) or scores.device.type != "cuda":
+        raise ValueError("scores must be a CUDA tensor")
+    if scores.dim() != 2:
+        raise ValueError(f"scores must be 2D, got {scores.dim()}D")
+    T, E = scores.shape
+    if top_k > E:
+        raise ValueError(f"top_k={top_k} > n_experts={E}")
+    if top_k < 1:
+        raise ValueError(f"top_k must be positive, got {top_k}")
+    if not 0.0 < threshold <= 1.0:
+        raise ValueError(f"threshold must be in (0, 1], got {threshold}")
+    s = scores.to(torch.float32).contiguous()
+    ids = torch.empty((T, top_k), dtype=torch.int32, device=s.device)
+    w = torch.empty((T, top_k), dtype=torch.float32, device=s.device)
+    n_kept = torch.empty(T, dtype=torch.int32, device=s.device)
+    flags = _lib.ROUTER_RENORMALIZE if renormalize else 0
+    _lib.check(_lib.lib().latent_router_topk(s.data_ptr(), T, E, top_k, float(threshold), flags, ids.data_ptr(),
+                                             w.data_ptr(), n_kept.data_ptr(), _stream_ptr(s.device)),
+               "latent_router_topk")
+    return ids, w, n_kept
 
 
 def moe_expert_ffn(x, ids, weights, experts: ExpertSet, weight_before_down: bool = False,

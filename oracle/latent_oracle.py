@@ -25,6 +25,8 @@ from typing import Dict, List, Mapping, Sequence, Tuple
 import numpy as np
 
 __all__ = [
+    "adaptive_keep",
+    "router_topk",
     "NF4_LEVELS",
     "nf4_encode",
     "nf4_decode",
@@ -306,3 +308,83 @@ def rel_l2(ref: np.ndarray, got: np.ndarray) -> float:
     got = np.asarray(got, dtype=np.float64)
     den = np.linalg.norm(ref)
     return float(np.linalg.norm(ref - got) / den) if den > 0 else float(np.linalg.norm(got))
+
+
+# --- adaptive top-k router (loader/adaptive_topk.py) -------------------------
+
+def _f32_sum(values: np.ndarray) -> np.float32:
+    """np.sum of a short float32 vector, written out: numpy's pairwise sum
+    (sequential from 0 below 8 elements; else eight strided accumulators
+    combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the tail)."""
+    a = np.asarray(values, np.float32)
+    n = a.size
+    if n < 8:
+        r = np.float32(0.0)
+        for v in a:
+            r = np.float32(r + v)
+        return r
+    acc = [np.float32(v) for v in a[:8]]
+    i = 8
+    while i < n - n % 8:
+        for j in range(8):
+            acc[j] = np.float32(acc[j] + a[i + j])
+        i += 8
+    r = np.float32(np.float32(np.float32(acc[0] + acc[1]) + np.float32(acc[2] + acc[3])) +
+                   np.float32(np.float32(acc[4] + acc[5]) + np.float32(acc[6] + acc[7])))
+    while i < n:
+        r = np.float32(r + a[i])
+        i += 1
+    return r
+
+
+def adaptive_keep(sorted_scores: np.ndarray, threshold: float = 0.95) -> Tuple[int, np.float32]:
+    """How many of the descending top-k scores to keep, and their float32 sum.
+
+    Restates adaptive_topk_inclusive (loader/adaptive_topk.py:29-56) with the
+    arithmetic numpy 2 gives it: total = float(np.sum(f32 scores)) (:47),
+    target = threshold * total in float64 (:51), then the running sum and the
+    comparison in float32 (a Python float meeting a float32 scalar is cast to
+    float32, :53-56)."""
+    s = np.asarray(sorted_scores, np.float32)
+    if s.size == 0:
+        return 0, np.float32(0.0)
+    if not 0.0 < threshold <= 1.0:
+        raise ValueError(f"threshold must be in (0, 1], got {threshold}")
+    total = float(_f32_sum(s))
+    if total <= 0:
+        return 0, np.float32(0.0)
+    target = np.float32(threshold * total)
+    cum = np.float32(0.0)
+    for i, v in enumerate(s):
+        if np.float32(cum + v) > target:
+            return i, cum
+        cum = np.float32(cum + v)
+    return int(s.size), cum
+
+
+def router_topk(scores: np.ndarray, top_k: int, threshold: float = 0.95, renormalize: bool = True):
+    """Router scores [T, E] -> (ids [T, k] int32, weights [T, k] float32, n_kept [T] int32).
+
+    Top-k selection in descending score order as adaptive_topk_batch
+    (loader/adaptive_topk.py:59-90; ties: lower expert id first, where the
+    reference's unstable argsort leaves the order open), then adaptive_keep
+    per token.  Dropped slots get id -1 and weight 0 (the op skips id < 0).
+    Kept weights are the scores divided by their float32 sum when
+    ``renormalize``, else the scores themselves."""
+    scores = np.asarray(scores, np.float32)
+    if scores.ndim != 2:
+        raise ValueError(f"scores must be 2D, got {scores.ndim}D")
+    T, E = scores.shape
+    if top_k > E:
+        raise ValueError(f"top_k={top_k} > n_experts={E}")
+    order = np.argsort(-scores, axis=1, kind="stable")[:, :top_k]
+    top = np.take_along_axis(scores, order, axis=1)
+    ids = np.full((T, top_k), -1, np.int32)
+    w = np.zeros((T, top_k), np.float32)
+    n_kept = np.zeros(T, np.int32)
+    for t in range(T):
+        n, cum = adaptive_keep(top[t], threshold)
+        n_kept[t] = n
+        ids[t, :n] = order[t, :n]
+        w[t, :n] = top[t, :n] / cum if renormalize else top[t, :n]
+    return ids, w, n_kept

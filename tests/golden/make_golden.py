@@ -17,6 +17,9 @@ Fixtures:
                encoders and SNR applied group by group
   runtime.npz  compress_matrix artifacts (reference NPZ keys) + swiglu_expert
                outputs, NF4 and whole-pair INT8, with/without weight_before_down
+  router.npz   adaptive_topk_batch (loader/adaptive_topk.py) on softmax router
+               scores: keep masks, kept counts and the reference's top-k order
+               for several (E, k, threshold), an all-zero row, k = E
   moe.npz      a small routed MoE layer: per-expert artifacts, x, ids (with -1
                slots), weights, per-slot outputs of the reference swiglu_expert
                and the fp64 top-k combine
@@ -201,6 +204,25 @@ def make_moe(ll, lr):
     np.savez_compressed(HERE / "moe.npz", **out)
 
 
+def make_router(ref_root: Path):
+    from loader import adaptive_topk as at  # noqa: E402
+    rng = np.random.default_rng(11)
+    out = {}
+    cases = [(8, 2, 0.95), (64, 6, 0.95), (64, 6, 0.5), (256, 8, 0.95), (256, 8, 1.0), (16, 16, 0.9),
+             (40, 12, 0.8)]
+    for c, (E, k, th) in enumerate(cases):
+        logits = rng.standard_normal((96, E)) * (1.0 + c % 3)
+        p = np.exp(logits - logits.max(axis=1, keepdims=True))
+        scores = (p / p.sum(axis=1, keepdims=True)).astype(np.float32)
+        scores[5] = 0.0                                   # total <= 0: nothing kept
+        keep, n_kept = at.adaptive_topk_batch(scores, k, th)
+        order = np.argsort(-scores, axis=1)[:, :k].astype(np.int32)
+        out.update({f"c{c}/scores": scores, f"c{c}/top_k": np.int32(k), f"c{c}/threshold": np.float64(th),
+                    f"c{c}/keep": keep, f"c{c}/n_kept": n_kept, f"c{c}/order": order})
+    out["n_cases"] = np.int32(len(cases))
+    np.savez_compressed(HERE / "router.npz", **out)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path, help="checkout of Yxmura/latent")
@@ -211,6 +233,7 @@ def main() -> int:
     make_mixed(ll)
     make_runtime(ll, lr)
     make_moe(ll, lr)
+    make_router(args.reference)
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
     return 0

@@ -80,3 +80,16 @@ def test_dequantize_and_silu_validate_on_host(lib):
     assert lib.latent_dequantize(C.byref(q), 0, None, None) == 1
     assert lib.latent_silu(None, None, -1, None) == 1
     assert lib.latent_silu(None, None, 0, None) == 0
+
+
+def test_router_topk_validates_on_host(lib):
+    f = lib.latent_router_topk
+    assert f(None, 4, 8, 9, 0.9, 0, None, None, None, None) == 2        # top_k > n_expert
+    assert f(None, 4, 8, 0, 0.9, 0, None, None, None, None) == 2        # top_k < 1
+    assert f(None, 4, 8, 2, 0.0, 0, None, None, None, None) == 1        # threshold outside (0, 1]
+    assert f(None, 4, 8, 2, 1.5, 0, None, None, None, None) == 1
+    assert f(None, 4, 8, 2, 0.9, 4, None, None, None, None) == 1        # unknown flag
+    assert f(None, 4, 2048, 2, 0.9, 0, None, None, None, None) == 9     # beyond 1024 experts
+    assert f(None, 4, 64, 33, 0.9, 0, None, None, None, None) == 9      # beyond top_k 32
+    assert f(None, 0, 8, 2, 0.9, 0, None, None, None, None) == 0        # empty batch: nothing to do
+    assert f(None, 4, 8, 2, 0.9, 0, None, None, None, None) == 1        # missing buffers

@@ -41,7 +41,7 @@ class CpuEPOps:
         import oracle as O
         y = np.zeros((rx.shape[0], rx.shape[1]), np.float32)
         lids = local_ids.numpy()[:, 0]
-        for e in np.unique(lids):
+        for e in np.unique(lids[lids >= 0]):
             rows = lids == e
             y[rows] = O.swiglu_expert(rx.numpy()[rows], *self.table[self.base + int(e)], rw.numpy()[rows, 0], wbd)
         return torch.from_numpy(y)
@@ -65,7 +65,7 @@ def _table(E, d, f, r):
     return [((mk(d, r), mk(r, f)), (mk(d, r), mk(r, f)), (mk(f, r), mk(r, d))) for _ in range(E)]
 
 
-def _worker(rank, world, port, outdir, wbd):
+def _worker(rank, world, port, outdir, wbd, max_tokens):
     sys.path.insert(0, str(ROOT))
     import oracle as O
     from latent_b200.ep import ExpertParallelFFN
@@ -82,11 +82,26 @@ def _worker(rank, world, port, outdir, wbd):
         ids[:, :] = np.where(ids >= 0, ids % 2, ids)   # rank 1 routes only to rank 0's experts
     w = rng.random((T, k)).astype(np.float32)
     ops = CpuEPOps(table, E, base=rank * (E // world))
-    ep = ExpertParallelFFN(E, ops)
+    ep = ExpertParallelFFN(E, ops, max_tokens=max_tokens)
     out = ep(torch.from_numpy(x), torch.from_numpy(ids), torch.from_numpy(w), weight_before_down=wbd).numpy()
     ref = O.moe_forward(x, ids, w, table, weight_before_down=wbd)
     np.save(Path(outdir) / f"r{rank}.npy", np.array([O.rel_l2(ref, out), float(sum(ep.last_counts[1]))]))
     dist.barrier()
+    dist.destroy_process_group()
+
+
+def _over_capacity(rank, world, port, outdir):
+    sys.path.insert(0, str(ROOT))
+    from latent_b200.ep import ExpertParallelFFN
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ep = ExpertParallelFFN(4, None, max_tokens=4)
+    try:
+        ep(torch.zeros((5, 8)), torch.zeros((5, 2), dtype=torch.int32), torch.ones((5, 2)))
+        msg = "no error"
+    except ValueError as e:
+        msg = str(e)
+    (Path(outdir) / f"r{rank}.txt").write_text(msg)
     dist.destroy_process_group()
 
 
@@ -98,13 +113,24 @@ def _free_port():
     return port
 
 
+@pytest.mark.parametrize("max_tokens", [None, 10, 16], ids=["exact", "cap10", "cap16"])
 @pytest.mark.parametrize("wbd", [False, True])
-def test_ep_two_cpu_ranks_match_single_process_oracle(wbd):
+def test_ep_two_cpu_ranks_match_single_process_oracle(wbd, max_tokens):
+    """Exact splits, and fixed-capacity blocks (10 = the larger batch; 16 leaves spare rows)."""
     world = 2
     with tempfile.TemporaryDirectory() as tmp:
-        mp.start_processes(_worker, args=(world, _free_port(), tmp, wbd), nprocs=world, join=True,
+        mp.start_processes(_worker, args=(world, _free_port(), tmp, wbd, max_tokens), nprocs=world, join=True,
                            start_method="spawn")
         res = [np.load(Path(tmp) / f"r{r}.npy") for r in range(world)]
     for rank, (err, n_recv) in enumerate(res):
         assert err < 1e-6, (rank, err)
     assert res[1][1] >= 0 and res[0][1] > 0   # rank 0 received rows from both ranks
+
+
+def test_ep_fixed_capacity_rejects_larger_batch():
+    world = 2
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.start_processes(_over_capacity, args=(world, _free_port(), tmp), nprocs=world, join=True,
+                           start_method="spawn")
+        for r in range(world):
+            assert "max_tokens" in (Path(tmp) / f"r{r}.txt").read_text()

@@ -23,7 +23,7 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-5
 
 
-def _worker(rank, world, port, outdir, wbd):
+def _worker(rank, world, port, outdir, wbd, max_tokens):
     sys.path.insert(0, str(ROOT))
     import datetime
     import torch.distributed as dist
@@ -44,7 +44,7 @@ def _worker(rank, world, port, outdir, wbd):
     ids[0, 1] = -1
     if rank == 1:
         ids = torch.where(ids >= 0, ids % e_local, ids)   # rank 1 sends only to rank 0
-    ep = ExpertParallelFFN(E, CudaEPOps(local, E))
+    ep = ExpertParallelFFN(E, CudaEPOps(local, E), max_tokens=max_tokens)
     errs = []
     for _ in range(2):                                   # the second call reuses the workspaces
         out = ep(x, ids, w, weight_before_down=wbd)
@@ -65,13 +65,14 @@ def _free_port():
 
 
 @pytest.mark.timeout(600)
+@pytest.mark.parametrize("max_tokens", [None, 64], ids=["exact", "fixed-capacity"])
 @pytest.mark.parametrize("wbd", [False, True])
-def test_ep_two_gpus_match_single_gpu(cuda, wbd):
+def test_ep_two_gpus_match_single_gpu(cuda, wbd, max_tokens):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     with tempfile.TemporaryDirectory() as tmp:
-        mp.start_processes(_worker, args=(world, _free_port(), tmp, wbd), nprocs=world, join=True,
+        mp.start_processes(_worker, args=(world, _free_port(), tmp, wbd, max_tokens), nprocs=world, join=True,
                            start_method="spawn")
         res = [np.load(Path(tmp) / f"r{r}.npy") for r in range(world)]
     for rank, r in enumerate(res):

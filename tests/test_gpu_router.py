@@ -1,0 +1,86 @@
+"""Adaptive top-k router on the GPU (latent_router_topk) against the
+reference's adaptive_topk_batch (loader/adaptive_topk.py:59-90, recorded in
+tests/golden/router.npz) and the oracle restatement.
+
+Integer outputs (ids, kept counts) are bit-exact; the renormalised weights
+are float32 divisions of the same operands on both sides, so they are
+compared bit for bit too."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import golden
+from latent_b200 import router_topk
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(scores, k, th, renorm=True):
+    ids, w, nk = router_topk(torch.from_numpy(scores).cuda(), k, th, renormalize=renorm)
+    return ids.cpu().numpy(), w.cpu().numpy(), nk.cpu().numpy()
+
+
+def test_router_matches_reference_golden(cuda):
+    z = golden("router")
+    for c in range(int(z["n_cases"])):
+        scores, k, th = z[f"c{c}/scores"], int(z[f"c{c}/top_k"]), float(z[f"c{c}/threshold"])
+        ids, w, nk = _run(scores, k, th)
+        keep = z[f"c{c}/keep"]
+        assert np.array_equal(nk, z[f"c{c}/n_kept"]), c
+        assert np.array_equal(ids >= 0, keep), c
+        assert np.array_equal(ids[keep], z[f"c{c}/order"][keep]), c
+        _, w_ref, _ = O.router_topk(scores, k, th)
+        assert np.array_equal(w.view(np.uint32), w_ref.view(np.uint32)), c
+
+
+@pytest.mark.parametrize("T,E,k,th", [(16384, 256, 8, 0.95), (333, 1024, 32, 0.9), (77, 1000, 6, 0.5),
+                                      (50, 1, 1, 1.0), (64, 64, 6, 1.0), (129, 33, 7, 0.7)])
+@pytest.mark.parametrize("renorm", [True, False])
+def test_router_matches_oracle(cuda, T, E, k, th, renorm):
+    rng = np.random.default_rng(T + E + k)
+    logits = rng.standard_normal((T, E)) * 2.0
+    p = np.exp(logits - logits.max(axis=1, keepdims=True))
+    scores = (p / p.sum(axis=1, keepdims=True)).astype(np.float32)
+    ids, w, nk = _run(scores, k, th, renorm)
+    ids_o, w_o, nk_o = O.router_topk(scores, k, th, renormalize=renorm)
+    assert np.array_equal(nk, nk_o)
+    assert np.array_equal(ids, ids_o)
+    assert np.array_equal(w.view(np.uint32), w_o.view(np.uint32))
+
+
+def test_router_ties_zero_rows_and_empty(cuda):
+    rng = np.random.default_rng(5)
+    scores = (rng.integers(0, 4, size=(200, 48)) / 8.0).astype(np.float32)   # many equal scores
+    scores[3] = 0.0
+    ids, w, nk = _run(scores, 6, 0.8)
+    ids_o, w_o, nk_o = O.router_topk(scores, 6, 0.8)
+    assert np.array_equal(ids, ids_o) and np.array_equal(nk, nk_o)
+    assert np.array_equal(w.view(np.uint32), w_o.view(np.uint32))
+    assert nk[3] == 0 and (ids[3] == -1).all()
+    ids, w, nk = router_topk(torch.empty((0, 16), device="cuda"), 2)
+    assert ids.shape == (0, 2) and nk.shape == (0,)
+
+
+def test_router_feeds_the_fused_op(cuda):
+    """Router output straight into the fused op equals the oracle MoE on the same routing."""
+    from latent_b200 import ExpertFFN, ExpertSet
+    from latent_b200 import format as F
+    z = golden("moe")
+    facs, pairs = [], []
+    for e in range(int(z["E"])):
+        arrays = {kk.split("/", 1)[1]: z[kk] for kk in z.files if kk.startswith(f"e{e}/")}
+        facs.append({f"{n}_{s}": F.from_npz(arrays, n, s) for n in ("gate", "up", "down") for s in ("a", "b")})
+        pairs.append(tuple(O.pair_from_npz(arrays, n) for n in ("gate", "up", "down")))
+    E = int(z["E"])
+    x = z["x"]
+    rng = np.random.default_rng(9)
+    logits = rng.standard_normal((x.shape[0], E))
+    p = np.exp(logits - logits.max(axis=1, keepdims=True))
+    scores = (p / p.sum(axis=1, keepdims=True)).astype(np.float32)
+    ids, w, _ = router_topk(torch.from_numpy(scores).cuda(), 2, 0.6)
+    y = ExpertFFN(ExpertSet(facs, device=torch.device("cuda", 0)), path="decode")(torch.from_numpy(x).cuda(), ids, w)
+    ids_o, w_o, _ = O.router_topk(scores, 2, 0.6)
+    ref = O.moe_forward(x, ids_o, w_o, pairs)
+    assert O.rel_l2(ref, y.cpu().numpy()) <= 1e-5

@@ -89,3 +89,25 @@ def test_route_is_stable_and_skips_negative_ids():
     assert counts.tolist() == [2, 2, 3, 0]
     assert offsets.tolist() == [0, 2, 4, 7, 7]
     assert order.tolist() == [1, 4, 6, 7, 0, 2, 5]
+
+
+def test_router_topk_matches_reference_adaptive_topk():
+    """oracle.router_topk vs adaptive_topk_batch (loader/adaptive_topk.py:59-90) on recorded cases."""
+    z = golden("router")
+    for c in range(int(z["n_cases"])):
+        scores, k, th = z[f"c{c}/scores"], int(z[f"c{c}/top_k"]), float(z[f"c{c}/threshold"])
+        ids, w, n_kept = O.router_topk(scores, k, th)
+        assert np.array_equal(n_kept, z[f"c{c}/n_kept"]), c
+        keep = z[f"c{c}/keep"]
+        assert np.array_equal(ids >= 0, keep), c
+        assert np.array_equal(ids[keep], z[f"c{c}/order"][keep]), c
+        live = n_kept > 0
+        assert np.allclose(w[live].sum(axis=1), 1.0, atol=1e-6)
+        assert not w[~keep].any()
+
+
+def test_router_topk_validates_like_reference():
+    with pytest.raises(ValueError):
+        O.router_topk(np.ones((2, 4), np.float32), 2, threshold=0.0)
+    with pytest.raises(ValueError):
+        O.router_topk(np.ones((2, 4), np.float32), 5)
