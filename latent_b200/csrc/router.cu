@@ -6,12 +6,14 @@
 // skips (kernels/latent_fused_expert_ffn.cu:33-40 treats id < 0 as a zero row).
 //
 // One warp per token.  Lane l holds scores l, l+32, ... of the row in
-// registers (coalesced 128-byte loads); k rounds of a warp arg-max (larger
-// score first, lower expert id on ties) produce the descending top-k, which
-// lane 0 then scans with the reference's arithmetic: the total is numpy's
+// registers (coalesced 128-byte loads) and tracks its best unselected one;
+// k rounds of a warp arg-max (two warp reductions: the largest order-
+// preserving key, then the lowest expert id holding it; only the winning
+// lane rescans) produce the descending top-k, which lane 0 then scans with
+// the reference's arithmetic: the total is numpy's
 // float32 pairwise sum, the target threshold x total is formed in double and
-// compared in float32, the running sum is float32.  HBM-bound: one read of the
-// scores, k ids + k weights written per token.
+// compared in float32, the running sum is float32.  Lane i writes slot i.
+// Traffic: one read of the scores, k ids + k weights written per token.
 #include "internal.h"
 
 namespace latent {
@@ -46,78 +48,95 @@ __device__ float f32_sum(const float *a, int n) {
     return r;
 }
 
+// Order-preserving 32-bit key of a score: a larger score has a larger key,
+// -0 and +0 share one key, and 0 is left for "nothing left to select".
+__device__ __forceinline__ unsigned score_key(float v) {
+    const unsigned b = v == 0.f ? 0u : __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 template <int NPL>
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(const float *__restrict__ scores, int T, int E,
                                                                     int k, double threshold, bool renorm,
                                                                     int *__restrict__ ids, float *__restrict__ weights,
                                                                     int *__restrict__ n_kept) {
     __shared__ float s_val[kRouterWarps][kMaxRouterTopK];
-    __shared__ int s_idx[kRouterWarps][kMaxRouterTopK];
+    const unsigned full = 0xffffffffu;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * kRouterWarps + warp;
     if (t >= T) return;
     const float *row = scores + (size_t)t * E;
     float v[NPL];
+    unsigned taken = 0;   // bit j: element j*32+lane selected, padding or NaN
 #pragma unroll
     for (int j = 0; j < NPL; ++j) {
         const int e = j * 32 + lane;
-        v[j] = e < E ? __ldg(row + e) : -INFINITY;
+        v[j] = e < E ? __ldg(row + e) : 0.f;
+        if (e >= E || v[j] != v[j]) taken |= 1u << j;
     }
-    unsigned taken = 0;
-    for (int r = 0; r < k; ++r) {
-        float bv = -INFINITY;
-        int bi = INT_MAX;
+    // each lane's best remaining element (lowest index among equal scores)
+    unsigned lkey = 0;
+    int lidx = INT_MAX;
+    float lval = 0.f;
+    auto rescan = [&]() {
+        lkey = 0;
+        lidx = INT_MAX;
 #pragma unroll
         for (int j = 0; j < NPL; ++j) {
-            const int e = j * 32 + lane;
-            const bool better = v[j] > bv || (v[j] == bv && e < bi);   // NaN never wins
-            if (e < E && !((taken >> j) & 1u) && better) {
-                bv = v[j];
-                bi = e;
+            const unsigned key = score_key(v[j]);
+            if (!((taken >> j) & 1u) && key > lkey) {
+                lkey = key;
+                lidx = j * 32 + lane;
+                lval = v[j];
             }
         }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-            }
+    };
+    rescan();
+    float my_val = 0.f;   // lane r keeps slot r
+    int my_idx = -1;
+    for (int r = 0; r < k; ++r) {
+        const unsigned m = __reduce_max_sync(full, lkey);
+        const unsigned win = __reduce_min_sync(full, lkey == m ? (unsigned)lidx : 0xffffffffu);
+        const bool none = m == 0u;
+        const float val = __shfl_sync(full, lval, none ? 0 : (int)(win & 31u));
+        if (!none && lane == (int)(win & 31u)) {
+            taken |= 1u << (win >> 5);
+            rescan();
         }
-        if (bi < E && (bi & 31) == lane) taken |= 1u << (bi >> 5);
-        if (lane == 0) {
-            s_val[warp][r] = bi < E ? bv : 0.f;
-            s_idx[warp][r] = bi < E ? bi : -1;
+        if (lane == r) {
+            my_val = none ? 0.f : val;
+            my_idx = none ? -1 : (int)win;
         }
+        if (lane == 0) s_val[warp][r] = none ? 0.f : val;
     }
-    __syncwarp();
-    if (lane != 0) return;
-    const float *sv = s_val[warp];
-    const int *si = s_idx[warp];
-    // adaptive_topk_inclusive (loader/adaptive_topk.py:46-56)
-    const float total = f32_sum(sv, k);
+    // adaptive_topk_inclusive (loader/adaptive_topk.py:46-56), by lane 0 in slot order
     int n = k;
     float cum = 0.f;
-    if (total <= 0.f) {
-        n = 0;
-    } else {
-        const float target = __double2float_rn(threshold * (double)total);
-        for (int i = 0; i < k; ++i) {
-            const float next = __fadd_rn(cum, sv[i]);
-            if (next > target) {
-                n = i;
-                break;
+    if (lane == 0) {
+        const float *sv = s_val[warp];
+        const float total = f32_sum(sv, k);
+        if (total <= 0.f) {
+            n = 0;
+        } else {
+            const float target = __double2float_rn(threshold * (double)total);
+            for (int i = 0; i < k; ++i) {
+                const float next = __fadd_rn(cum, sv[i]);
+                if (next > target) {
+                    n = i;
+                    break;
+                }
+                cum = next;
             }
-            cum = next;
         }
     }
-    for (int i = 0; i < k; ++i) {
-        const bool keep = i < n && si[i] >= 0;
-        ids[(size_t)t * k + i] = keep ? si[i] : -1;
-        weights[(size_t)t * k + i] = keep ? (renorm ? __fdiv_rn(sv[i], cum) : sv[i]) : 0.f;
+    n = __shfl_sync(full, n, 0);
+    cum = __shfl_sync(full, cum, 0);
+    if (lane < k) {
+        const bool keep = lane < n && my_idx >= 0;
+        ids[(size_t)t * k + lane] = keep ? my_idx : -1;
+        weights[(size_t)t * k + lane] = keep ? (renorm ? __fdiv_rn(my_val, cum) : my_val) : 0.f;
     }
-    if (n_kept) n_kept[t] = n;
+    if (lane == 0 && n_kept) n_kept[t] = n;
 }
 
 template <int NPL>
