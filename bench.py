@@ -63,8 +63,9 @@ def parse_args():
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill leg of the default run")
     ap.add_argument("--ep-exact", action="store_true",
                     help="expert parallel: exact splits with a host read of the counts (default: fixed capacity)")
-    ap.add_argument("--ep-graph", action="store_true",
-                    help="expert parallel: replay the fixed-capacity step as one captured CUDA graph")
+    ap.add_argument("--ep-eager", action="store_true",
+                    help="expert parallel: launch the fixed-capacity step eagerly instead of replaying it "
+                         "as one captured CUDA graph (the default)")
     return ap.parse_args()
 
 
@@ -471,7 +472,7 @@ def run_ours_ep(args, world, rank, local):
     torch.cuda.synchronize()
     step = lambda: ep(x, ids, w)
     graph = None
-    if args.ep_graph and not args.ep_exact:
+    if not args.ep_eager and not args.ep_exact:
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
@@ -559,7 +560,7 @@ def run_ours_ep(args, world, rank, local):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE recipe)",
         "config": config_json(cfg, ids, world, f"expert-parallel ep{world} (NCCL all-to-all, "
                               f"{'exact splits' if args.ep_exact else 'fixed capacity'}"
-                              f"{', CUDA graph' if args.ep_graph and not args.ep_exact else ''})"),
+                              f"{', CUDA graph' if not args.ep_eager and not args.ep_exact else ''})"),
         "roofline": {"bound": "hbm", "kernel": "local fused expert FFN (rank 0)", "achieved": ach,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "traffic": None,
                      "algorithmic_bytes": local_bytes, "mean_ms": ffn_ms, "peak_source": pk["source"]},

@@ -48,8 +48,9 @@ __device__ float f32_sum(const float *a, int n) {
     return r;
 }
 
-// Order-preserving 32-bit key of a score: a larger score has a larger key,
-// -0 and +0 share one key, and 0 is left for "nothing left to select".
+// Order-preserving 32-bit key of a finite or infinite score: a larger score
+// has a larger key, -0 and +0 share one key, and no score maps to 0 (the
+// mark for "nothing left to select").
 __device__ __forceinline__ unsigned score_key(float v) {
     const unsigned b = v == 0.f ? 0u : __float_as_uint(v);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
@@ -67,40 +68,44 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(const float *
     if (t >= T) return;
     const float *row = scores + (size_t)t * E;
     float v[NPL];
-    unsigned taken = 0;   // bit j: element j*32+lane selected, padding or NaN
+    unsigned key[NPL];    // 0: padding, NaN or already selected
 #pragma unroll
     for (int j = 0; j < NPL; ++j) {
         const int e = j * 32 + lane;
         v[j] = e < E ? __ldg(row + e) : 0.f;
-        if (e >= E || v[j] != v[j]) taken |= 1u << j;
+        key[j] = (e >= E || v[j] != v[j]) ? 0u : score_key(v[j]);
     }
     // each lane's best remaining element (lowest index among equal scores)
     unsigned lkey = 0;
-    int lidx = INT_MAX;
-    float lval = 0.f;
+    int lj = 0;
     auto rescan = [&]() {
         lkey = 0;
-        lidx = INT_MAX;
+        lj = 0;
 #pragma unroll
         for (int j = 0; j < NPL; ++j) {
-            const unsigned key = score_key(v[j]);
-            if (!((taken >> j) & 1u) && key > lkey) {
-                lkey = key;
-                lidx = j * 32 + lane;
-                lval = v[j];
+            if (key[j] > lkey) {
+                lkey = key[j];
+                lj = j;
             }
         }
+    };
+    auto value_at = [&](int jj) {
+        float x = v[0];
+#pragma unroll
+        for (int j = 1; j < NPL; ++j) x = jj == j ? v[j] : x;
+        return x;
     };
     rescan();
     float my_val = 0.f;   // lane r keeps slot r
     int my_idx = -1;
     for (int r = 0; r < k; ++r) {
         const unsigned m = __reduce_max_sync(full, lkey);
-        const unsigned win = __reduce_min_sync(full, lkey == m ? (unsigned)lidx : 0xffffffffu);
+        const unsigned win = __reduce_min_sync(full, lkey == m ? (unsigned)(lj * 32 + lane) : 0xffffffffu);
         const bool none = m == 0u;
-        const float val = __shfl_sync(full, lval, none ? 0 : (int)(win & 31u));
+        const float val = __shfl_sync(full, value_at(lj), none ? 0 : (int)(win & 31u));
         if (!none && lane == (int)(win & 31u)) {
-            taken |= 1u << (win >> 5);
+#pragma unroll
+            for (int j = 0; j < NPL; ++j) key[j] = j == lj ? 0u : key[j];
             rescan();
         }
         if (lane == r) {
