@@ -17,6 +17,12 @@ Fixtures:
                encoders and SNR applied group by group
   runtime.npz  compress_matrix artifacts (reference NPZ keys) + swiglu_expert
                outputs, NF4 and whole-pair INT8, with/without weight_before_down
+  latent_layer.gguf + gguf_layer.npz
+               one MoE layer stacked by the reference's compress_layer_to_stacked
+               (loader/write_latent_gguf.py:126-275) and written with its tensor
+               names and byte layout (:412-436); the npz holds the reference
+               dequantized factors of every expert and a routed batch with the
+               reference swiglu_expert outputs combined in fp64
   router.npz   adaptive_topk_batch (loader/adaptive_topk.py) on softmax router
                scores: keep masks, kept counts and the reference's top-k order
                for several (E, k, threshold), an all-zero row, k = E
@@ -223,6 +229,64 @@ def make_router(ref_root: Path):
     np.savez_compressed(HERE / "router.npz", **out)
 
 
+def make_gguf(ll, lr, ref_root: Path):
+    import gguf
+    from loader import write_latent_gguf as wl  # noqa: E402
+    rng = np.random.default_rng(21)
+    E, d, f, layer = 3, 64, 96, 5
+    # numpy write order of the GGUF reader: (n_out, n_in, n_expert)
+    gate = np.stack([_spectral(rng, d, f, 32).T for _ in range(E)], axis=2).astype(np.float32)
+    up = np.stack([_spectral(rng, d, f, 32).T for _ in range(E)], axis=2).astype(np.float32)
+    down = np.stack([_spectral(rng, f, d, 32).T for _ in range(E)], axis=2).astype(np.float32)
+    wt, st, reports, ranks = wl.compress_layer_to_stacked(
+        layer_idx=layer, gate_exps=gate, up_exps=up, down_exps=down, energy=0.9, min_rank=8, max_rank=32,
+        group_size=32, int8_group_size=64, error_threshold=10.0, snr_threshold=0.0,
+        low_snr_fraction_threshold=1.0)
+    w = gguf.GGUFWriter(str(HERE / "latent_layer.gguf"), arch="deepseek4", use_temp_file=False)
+    for name, arr in wt.items():           # same byte layout as write_latent_gguf.py:426-431
+        w.add_tensor(name, arr.astype(np.int8).reshape(arr.shape[2], arr.shape[1], arr.shape[0]),
+                     raw_dtype=gguf.GGMLQuantizationType.I8)
+    for name, arr in st.items():
+        w.add_tensor(name, arr.astype(np.float16).reshape(arr.shape[2], arr.shape[1], arr.shape[0]),
+                     raw_dtype=gguf.GGMLQuantizationType.F16)
+    w.add_tensor(f"blk.{layer}.ffn_latent_ranks", ranks.T.astype(np.uint8), raw_dtype=gguf.GGMLQuantizationType.I8)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    out = {"E": np.int32(E), "layer": np.int32(layer), "ranks": ranks}
+    dense = {}
+    for kind in ("gate", "up", "down"):
+        for ab in ("a", "b"):
+            codes, scales = wt[f"blk.{layer}.ffn_latent_{kind}_{ab}"], st[f"blk.{layer}.ffn_latent_{kind}_{ab}_s"]
+            n_e, rows, half = codes.shape
+            for e in range(E):
+                vals = np.stack([ll.dequantize_nf4(codes[e, i], scales[e, i], (2 * half,), group_size=32)
+                                 for i in range(rows)])
+                dense[(e, kind, ab)] = vals.astype(np.float32)
+                out[f"e{e}/{kind}_{ab}"] = dense[(e, kind, ab)]
+    T, k = 12, 2
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    ids = rng.integers(0, E, size=(T, k)).astype(np.int32)
+    ids[1, 1] = -1
+    wts = rng.random((T, k)).astype(np.float32)
+    res = np.zeros((T, d), np.float64)
+    for t in range(T):
+        for j in range(k):
+            e = int(ids[t, j])
+            if e < 0:
+                continue
+            pr = []
+            for kind in ("gate", "up", "down"):
+                a, b = dense[(e, kind, "a")], dense[(e, kind, "b")]
+                r = min(a.shape[1], b.shape[0])     # B rows = the largest actual rank; A cols = max_rank
+                pr.append(lr.FactorPair(a[:, :r], b[:r]))
+            y = lr.swiglu_expert(x[t:t + 1], *pr)
+            res[t] += float(wts[t, j]) * y[0].astype(np.float64)
+    out.update(x=x, ids=ids, weights=wts, out=res.astype(np.float32))
+    np.savez_compressed(HERE / "gguf_layer.npz", **out)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path, help="checkout of Yxmura/latent")
@@ -234,6 +298,7 @@ def main() -> int:
     make_runtime(ll, lr)
     make_moe(ll, lr)
     make_router(args.reference)
+    make_gguf(ll, lr, args.reference)
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
     return 0
