@@ -450,6 +450,9 @@ class _TimedOps:
     def combine(self, *a):
         return self.ops.combine(*a)
 
+    def __getattr__(self, name):   # the fixed-capacity pack/combine of the wrapped ops
+        return getattr(self.ops, name)
+
 
 def run_ours_ep(args, world, rank, local):
     """Expert-parallel step on `world` GPUs: experts sharded contiguously, a full config batch per rank

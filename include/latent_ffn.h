@@ -175,6 +175,22 @@ LATENT_API int latent_ep_workspace_size(const latent_ep_desc *desc, size_t *byte
 LATENT_API int latent_ep_dispatch(const latent_ep_desc *desc, struct CUstream_st *stream);
 LATENT_API int latent_ep_combine(const latent_ep_desc *desc, struct CUstream_st *stream);
 
+/* Fixed-capacity exchange blocks (no counterpart in the reference, which has
+ * no multi-GPU code).  After latent_ep_dispatch on the same desc and
+ * workspace, latent_ep_pack_fixed writes send_rows[world*cap][d] (x's type):
+ * block g holds, in routed order, the rows routed to rank g's experts
+ * [g*E/world, (g+1)*E/world); send_meta[world*cap][2] int32 holds
+ * {global expert id, router weight bits} per row, {-1, 0} for unused rows.
+ * cap must be at least the rows any destination receives (T*min(k, E/world)
+ * when a token routes no expert twice).  latent_ep_combine_fixed reads the
+ * returned blocks y_rows[world*cap][d] fp32 (same placement) and writes
+ * out[T][d] = sum_j w[t,j] * y (plain sum with LATENT_FLAG_WEIGHT_BEFORE_DOWN).
+ * Neither needs the host to know the per-destination counts. */
+LATENT_API int latent_ep_pack_fixed(const latent_ep_desc *desc, int32_t world, int32_t cap, void *send_rows,
+                                    int32_t *send_meta, struct CUstream_st *stream);
+LATENT_API int latent_ep_combine_fixed(const latent_ep_desc *desc, int32_t world, int32_t cap, const float *y_rows,
+                                       float *out, struct CUstream_st *stream);
+
 /* ABI version of the loaded library (LATENT_ABI_VERSION). */
 LATENT_API int latent_abi_version(void);
 

@@ -106,6 +106,9 @@ EXPORTS.update({
     "latent_expert_ffn_forward_timed": (C.c_int, [C.POINTER(FfnDesc), C.c_void_p, C.POINTER(C.c_void_p), C.c_int]),
     "latent_dequantize": (C.c_int, [C.POINTER(QMatrix), C.c_int32, C.c_void_p, C.c_void_p]),
     "latent_silu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
+    "latent_ep_pack_fixed": (C.c_int, [C.POINTER(EpDesc), C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "latent_ep_combine_fixed": (C.c_int, [C.POINTER(EpDesc), C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
+                                          C.c_void_p]),
     "latent_router_topk": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_double, C.c_uint32,
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "latent_pack_tiles": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p,

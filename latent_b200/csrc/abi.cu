@@ -352,6 +352,69 @@ extern "C" LATENT_API int latent_ep_dispatch(const latent_ep_desc *desc, CUstrea
     return cuda_status(launch_ep_gather(e, s));
 }
 
+namespace latent {
+namespace {
+
+int ep_fixed_check(const latent_ep_desc *d, int32_t world, int32_t cap) {
+    const int st = ep_validate(d);
+    if (st) return st;
+    if (world < 1 || d->n_expert % world || cap < 1 || (int64_t)world * cap > (int64_t)1 << 30)
+        return LATENT_ERR_SHAPE;
+    if (!d->workspace || d->workspace_bytes < ep_layout(d).total) return LATENT_ERR_WORKSPACE;
+    if (!aligned(d->workspace, kAlign)) return LATENT_ERR_ALIGN;
+    return LATENT_OK;
+}
+
+EpArgs ep_args(const latent_ep_desc *d) {
+    const Layout L = ep_layout(d);
+    EpArgs e{};
+    e.E = d->n_expert;
+    e.d = d->n_embd;
+    e.T = d->n_tokens;
+    e.k = d->top_k;
+    e.x_type = d->x_type;
+    e.w_type = d->w_type;
+    e.x = d->x;
+    e.ids = d->ids;
+    e.weights = d->weights;
+    e.offsets = at<int32_t>(d->workspace, L.offsets);
+    e.order = at<int32_t>(d->workspace, L.order);
+    e.send_x = d->send_x;
+    e.send_expert = d->send_expert;
+    e.send_weight = d->send_weight;
+    return e;
+}
+
+}  // namespace
+}  // namespace latent
+
+extern "C" LATENT_API int latent_ep_pack_fixed(const latent_ep_desc *desc, int32_t world, int32_t cap, void *send_rows,
+                                               int32_t *send_meta, CUstream_st *stream) {
+    int st = ep_fixed_check(desc, world, cap);
+    if (st) return st;
+    if (!send_rows || !send_meta) return LATENT_ERR_INVALID;
+    if (!aligned(send_rows, 16) || !aligned(send_meta, 8)) return LATENT_ERR_ALIGN;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (desc->n_tokens == 0)   // latent_ep_dispatch routed nothing: every row is unused
+        return cuda_status(cudaMemsetAsync(send_meta, 0xff, (size_t)world * cap * 8, s));
+    if (!desc->send_x || !desc->send_expert || !desc->send_weight) return LATENT_ERR_INVALID;
+    if (!aligned(desc->send_x, 16)) return LATENT_ERR_ALIGN;
+    return cuda_status(launch_ep_pack_fixed(ep_args(desc), world, cap, send_rows, send_meta, s));
+}
+
+extern "C" LATENT_API int latent_ep_combine_fixed(const latent_ep_desc *desc, int32_t world, int32_t cap,
+                                                  const float *y_rows, float *out, CUstream_st *stream) {
+    int st = ep_fixed_check(desc, world, cap);
+    if (st) return st;
+    if (desc->n_tokens == 0) return LATENT_OK;
+    if (!y_rows || !out || !desc->ids || !desc->weights) return LATENT_ERR_INVALID;
+    if (!aligned(y_rows, 16) || !aligned(out, 16)) return LATENT_ERR_ALIGN;
+    const Layout L = ep_layout(desc);
+    return cuda_status(launch_ep_combine_fixed(ep_args(desc), at<int32_t>(desc->workspace, L.pos), world, cap, y_rows,
+                                               out, (desc->flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN) != 0,
+                                               reinterpret_cast<cudaStream_t>(stream)));
+}
+
 extern "C" LATENT_API int latent_ep_combine(const latent_ep_desc *desc, CUstream_st *stream) {
     int st = ep_validate(desc);
     if (st) return st;

@@ -1,8 +1,9 @@
 // Expert-parallel dispatch and combine (no counterpart in the reference,
 // which has no multi-GPU code).  The rows a rank sends travel through NCCL
 // all-to-all in the caller; these kernels only pack them in expert order
-// (which is destination-rank order, experts being contiguous per rank) and
-// fold the returned expert outputs into the top-k combine.
+// (which is destination-rank order, experts being contiguous per rank),
+// optionally into fixed-capacity blocks per destination rank, and fold the
+// returned expert outputs into the top-k combine.
 #include "internal.h"
 
 namespace latent {
@@ -29,7 +30,78 @@ __global__ void __launch_bounds__(128) k_ep_gather(EpArgs a) {
     }
 }
 
+// Fixed-capacity block q of the send buffer: block g = q / cap holds the
+// rows routed to rank g's experts [g*el, (g+1)*el) in routed order, rows past
+// their count get expert id -1.  One block per padded row.
+template <int XT>
+__global__ void __launch_bounds__(128) k_ep_pack_fixed(EpArgs a, int el, int cap, void *rows, int32_t *meta) {
+    const int q = blockIdx.x;
+    const int g = q / cap, i = q - g * cap;
+    const int p = a.offsets[g * el] + i;
+    const bool valid = p < a.offsets[(g + 1) * el];
+    if (threadIdx.x == 0) {
+        meta[2 * q] = valid ? a.send_expert[p] : -1;
+        meta[2 * q + 1] = valid ? __float_as_int(a.send_weight[p]) : 0;
+    }
+    if (!valid) return;
+    const size_t es = XT == LATENT_TYPE_F32 ? 4 : 2;
+    const char *src = static_cast<const char *>(a.send_x) + (size_t)p * a.d * es;
+    char *dst = static_cast<char *>(rows) + (size_t)q * a.d * es;
+    const int n16 = (int)(a.d * es / 16);
+    for (int j = threadIdx.x; j < n16; j += blockDim.x)
+        reinterpret_cast<uint4 *>(dst)[j] = __ldg(reinterpret_cast<const uint4 *>(src) + j);
+}
+
+// out[t] = sum_j w[t,j] * y_rows[block row of slot (t,j)], the inverse of
+// k_ep_pack_fixed's placement (row = g*cap + routed position - first
+// position of rank g).  Skipped slots (id < 0), out-of-range ids and rows
+// that did not fit their block contribute nothing.
+__global__ void __launch_bounds__(256) k_ep_combine_fixed(EpArgs a, const int32_t *pos, int el, int cap,
+                                                          const float *y, float *out, bool wbd) {
+    const int t = blockIdx.y;
+    const int c = (blockIdx.x * 256 + threadIdx.x) * 4;
+    if (c >= a.d) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < a.k; ++j) {
+        const int slot = t * a.k + j;
+        const int e = __ldg(a.ids + slot);
+        if (e < 0 || e >= a.E) continue;
+        const int p = pos[slot];
+        if (p < 0) continue;
+        const int g = e / el;
+        const int i = p - a.offsets[g * el];
+        if (i < 0 || i >= cap) continue;   // beyond the block: never sent (cap too small)
+        const int q = g * cap + i;
+        const float w = wbd ? 1.f : load_weight(a.weights, a.w_type, slot);
+        const float4 v = *reinterpret_cast<const float4 *>(y + (int64_t)q * a.d + c);
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+    }
+    *reinterpret_cast<float4 *>(out + (int64_t)t * a.d + c) = acc;
+}
+
 }  // namespace
+
+cudaError_t launch_ep_pack_fixed(const EpArgs &a, int world, int cap, void *rows, int32_t *meta, cudaStream_t s) {
+    const int n = world * cap;
+    const int el = a.E / world;
+    switch (a.x_type) {
+        case LATENT_TYPE_F32: k_ep_pack_fixed<LATENT_TYPE_F32><<<n, 128, 0, s>>>(a, el, cap, rows, meta); break;
+        case LATENT_TYPE_F16: k_ep_pack_fixed<LATENT_TYPE_F16><<<n, 128, 0, s>>>(a, el, cap, rows, meta); break;
+        default: k_ep_pack_fixed<LATENT_TYPE_BF16><<<n, 128, 0, s>>>(a, el, cap, rows, meta); break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_combine_fixed(const EpArgs &a, const int32_t *pos, int world, int cap, const float *y, float *out,
+                                    bool wbd, cudaStream_t s) {
+    if (a.T == 0) return cudaSuccess;
+    dim3 grid((a.d / 4 + 255) / 256, a.T);
+    k_ep_combine_fixed<<<grid, 256, 0, s>>>(a, pos, a.E / world, cap, y, out, wbd);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_ep_gather(const EpArgs &a, cudaStream_t s) {
     const int rows = a.T * a.k;

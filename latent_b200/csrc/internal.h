@@ -128,6 +128,9 @@ struct EpArgs {
 };
 
 cudaError_t launch_ep_gather(const EpArgs &a, cudaStream_t s);
+cudaError_t launch_ep_pack_fixed(const EpArgs &a, int world, int cap, void *rows, int32_t *meta, cudaStream_t s);
+cudaError_t launch_ep_combine_fixed(const EpArgs &a, const int32_t *pos, int world, int cap, const float *y, float *out,
+                                    bool wbd, cudaStream_t s);
 
 cudaError_t launch_dequant(const latent_qmatrix &m, int expert, float *out, cudaStream_t s);
 cudaError_t launch_silu(const float *x, float *y, int64_t n, cudaStream_t s);

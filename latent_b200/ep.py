@@ -85,6 +85,25 @@ class CudaEPOps:
             return torch.empty((0, rx.shape[1]), dtype=torch.float32, device=rx.device)
         return self.ffn(rx, local_ids, rw, weight_before_down=wbd)
 
+    def pack_fixed(self, p: Packed, world: int, cap: int):
+        """Fixed-capacity send blocks: rows [world*cap, d] and meta [world*cap, 2] (id -1 marks unused rows)."""
+        x, ids, weights, wbd = p.state
+        rows = torch.empty((world * cap, x.shape[1]), dtype=x.dtype, device=x.device)
+        meta = torch.empty((world * cap, 2), dtype=torch.int32, device=x.device)
+        d = self._desc(x, ids, weights, wbd)
+        d.send_x, d.send_expert, d.send_weight = p.send_x.data_ptr(), p.send_expert.data_ptr(), p.send_weight.data_ptr()
+        _lib.check(_lib.lib().latent_ep_pack_fixed(C.byref(d), world, cap, rows.data_ptr(), meta.data_ptr(),
+                                                   _stream_ptr(x.device)), "latent_ep_pack_fixed")
+        return rows, meta
+
+    def combine_fixed(self, p: Packed, y_rows: torch.Tensor, world: int, cap: int) -> torch.Tensor:
+        x, ids, weights, wbd = p.state
+        out = torch.empty((ids.shape[0], x.shape[1]), dtype=torch.float32, device=x.device)
+        d = self._desc(x, ids, weights, wbd)
+        _lib.check(_lib.lib().latent_ep_combine_fixed(C.byref(d), world, cap, y_rows.data_ptr(), out.data_ptr(),
+                                                      _stream_ptr(x.device)), "latent_ep_combine_fixed")
+        return out
+
     def combine(self, p: Packed, y_back: torch.Tensor) -> torch.Tensor:
         x, ids, weights, wbd = p.state
         out = torch.empty((ids.shape[0], x.shape[1]), dtype=torch.float32, device=x.device)
@@ -173,21 +192,18 @@ class ExpertParallelFFN:
         cap = self.max_tokens * min(k, self.e_local)
         dev = x.device
         p = self.ops.dispatch(x, ids, weights, wbd)
-        P = p.send_x.shape[0]
         send_counts = p.expert_counts.view(G, self.e_local).sum(dim=1).to(torch.int64)
-        end = torch.cumsum(send_counts, 0)
-        if self._pos is None or self._pos.numel() < P or self._pos.device != dev:
-            self._pos = torch.arange(max(P, 1), dtype=torch.int64, device=dev)
-        pos = self._pos[:P]
-        g = torch.searchsorted(end, pos, right=True)             # destination rank; G past the routed rows
-        gc = g.clamp(max=G - 1)
-        slot = pos - (end - send_counts)[gc]
-        dst = torch.where(g < G, gc * cap + slot, torch.full_like(pos, G * cap))   # row G*cap: discard
-        send_x = torch.empty((G * cap + 1, d), dtype=x.dtype, device=dev)
-        send_x.index_copy_(0, dst, p.send_x)
-        meta = torch.stack([p.send_expert[:P], p.send_weight[:P].view(torch.int32)], dim=1)
-        send_meta = torch.full((G * cap + 1, 2), -1, dtype=torch.int32, device=dev)
-        send_meta.index_copy_(0, dst, meta)
+        fused = hasattr(self.ops, "pack_fixed")
+        if fused:
+            send_x, send_meta = self.ops.pack_fixed(p, G, cap)
+        else:
+            # the same placement from torch index kernels (ops without a fused pack, e.g. CPU test doubles)
+            dst = self._fixed_rows(p, send_counts, G, cap)
+            send_x = torch.empty((G * cap + 1, d), dtype=x.dtype, device=dev)
+            send_x.index_copy_(0, dst, p.send_x)
+            meta = torch.stack([p.send_expert[:dst.numel()], p.send_weight[:dst.numel()].view(torch.int32)], dim=1)
+            send_meta = torch.full((G * cap + 1, 2), -1, dtype=torch.int32, device=dev)
+            send_meta.index_copy_(0, dst, meta)
         recv_x = torch.empty((G * cap, d), dtype=x.dtype, device=dev)
         dist.all_to_all_single(recv_x, send_x[:G * cap], group=self.group)
         recv_meta = torch.empty((G * cap, 2), dtype=torch.int32, device=dev)
@@ -201,6 +217,20 @@ class ExpertParallelFFN:
         y = self.ops.local_ffn(recv_x, local_ids, rw, wbd)
         y_pad = torch.empty((G * cap, d), dtype=torch.float32, device=dev)
         dist.all_to_all_single(y_pad, y.contiguous(), group=self.group)
-        y_back = y_pad.index_select(0, dst.clamp(max=G * cap - 1))
         self._counts = (send_counts, (rid.view(G, cap) >= 0).sum(dim=1))
-        return self.ops.combine(p, y_back)
+        if fused:
+            return self.ops.combine_fixed(p, y_pad, G, cap)
+        return self.ops.combine(p, y_pad.index_select(0, dst.clamp(max=G * cap - 1)))
+
+    def _fixed_rows(self, p, send_counts, G: int, cap: int) -> torch.Tensor:
+        """Block row of every routed position (G*cap past the routed rows: a discard row)."""
+        P = p.send_x.shape[0]
+        dev = p.send_x.device
+        if self._pos is None or self._pos.numel() < P or self._pos.device != dev:
+            self._pos = torch.arange(max(P, 1), dtype=torch.int64, device=dev)
+        pos = self._pos[:P]
+        end = torch.cumsum(send_counts, 0)
+        g = torch.searchsorted(end, pos, right=True)
+        gc = g.clamp(max=G - 1)
+        slot = pos - (end - send_counts)[gc]
+        return torch.where(g < G, gc * cap + slot, torch.full_like(pos, G * cap))
