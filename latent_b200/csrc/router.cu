@@ -62,6 +62,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(const float *
                                                                     int *__restrict__ ids, float *__restrict__ weights,
                                                                     int *__restrict__ n_kept) {
     __shared__ float s_val[kRouterWarps][kMaxRouterTopK];
+    __shared__ int s_idx[kRouterWarps][kMaxRouterTopK];
     const unsigned full = 0xffffffffu;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * kRouterWarps + warp;
@@ -96,24 +97,26 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(const float *
         return x;
     };
     rescan();
-    float my_val = 0.f;   // lane r keeps slot r
-    int my_idx = -1;
     for (int r = 0; r < k; ++r) {
         const unsigned m = __reduce_max_sync(full, lkey);
         const unsigned win = __reduce_min_sync(full, lkey == m ? (unsigned)(lj * 32 + lane) : 0xffffffffu);
         const bool none = m == 0u;
-        const float val = __shfl_sync(full, value_at(lj), none ? 0 : (int)(win & 31u));
+        // the score back from its key; a zero score takes the winner's own bits (keeps the sign of -0)
+        float val = __uint_as_float((m & 0x80000000u) ? (m & 0x7fffffffu) : ~m);
+        if (m == 0x80000000u) val = __shfl_sync(full, value_at(lj), (int)(win & 31u));
         if (!none && lane == (int)(win & 31u)) {
 #pragma unroll
             for (int j = 0; j < NPL; ++j) key[j] = j == lj ? 0u : key[j];
             rescan();
         }
-        if (lane == r) {
-            my_val = none ? 0.f : val;
-            my_idx = none ? -1 : (int)win;
+        if (lane == 0) {
+            s_val[warp][r] = none ? 0.f : val;
+            s_idx[warp][r] = none ? -1 : (int)win;
         }
-        if (lane == 0) s_val[warp][r] = none ? 0.f : val;
     }
+    __syncwarp();
+    const float my_val = lane < k ? s_val[warp][lane] : 0.f;   // lane i writes slot i
+    const int my_idx = lane < k ? s_idx[warp][lane] : -1;
     // adaptive_topk_inclusive (loader/adaptive_topk.py:46-56), by lane 0 in slot order
     int n = k;
     float cum = 0.f;
