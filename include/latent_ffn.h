@@ -39,7 +39,8 @@
  *   i8_hi   uint8  [n_int8_groups][16]        high nibbles of the INT8
  *                                              groups in (expert, q) order,
  *                                              same nibble order as codes
- * i8_mask/i8_base/i8_hi are NULL when no group is INT8.  The tile order lets
+ * i8_mask/i8_base/i8_hi are NULL when no group is INT8; otherwise all three
+ * start on a 16-byte boundary (codes and scales too).  The tile order lets
  * a kernel streaming a row range of one column tile read its codes, scales
  * and INT8 records as three contiguous runs (latent_b200/format.py packs it).
  * cols must be a multiple of 32; the rank dimension may be zero-padded

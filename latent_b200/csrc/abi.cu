@@ -43,7 +43,8 @@ int check_qmatrix(const latent_qmatrix &m, int64_t rows, int64_t cols, bool need
     if (!aligned(m.codes, 16) || !aligned(m.scales, 16)) return LATENT_ERR_ALIGN;
     const bool any = m.i8_mask || m.i8_base || m.i8_hi;
     if (any && !(m.i8_mask && m.i8_base && m.i8_hi)) return LATENT_ERR_INVALID;
-    if (m.i8_hi && !aligned(m.i8_hi, 16)) return LATENT_ERR_ALIGN;
+    if (m.i8_hi && (!aligned(m.i8_hi, 16) || !aligned(m.i8_mask, 16) || !aligned(m.i8_base, 16)))
+        return LATENT_ERR_ALIGN;
     return LATENT_OK;
 }
 

@@ -12,13 +12,12 @@ namespace latent {
 constexpr int kRouteSingleMax = 4096;  // routed slots served by one routing block
 constexpr int kRouteChunk = 8192;      // slots per block in the multi-block routing
 constexpr int kMaxExperts = 1024;
-constexpr int kVirtTokens = 4;         // routed positions per virtual expert (decode path)
+constexpr int kVirtTokens = 8;         // routed positions per virtual expert (decode path)
 
-// Relative decode cost of a virtual expert of nt tokens; the decode kernel
-// balances its warps by these weights.  Its inner loop runs one code path
-// for up to kVirtTokens tokens (fewer are zero-padded), so the cost per
-// byte does not depend on nt.
-__host__ __device__ constexpr int virt_weight(int nt) { return nt > 0 ? 1 : 0; }
+// Token columns of a virtual expert of nt routed positions: the decode
+// kernel runs 4-column and 8-column code paths (fewer positions are
+// zero-padded), and lays its intermediates out with this many columns.
+__host__ __device__ constexpr int virt_weight(int nt) { return nt <= 0 ? 0 : nt <= 4 ? 4 : 8; }
 
 struct RouteArgs {
     const int32_t *ids;
@@ -39,8 +38,8 @@ struct RouteArgs {
     int n_blocks;
     // Virtual experts (decode path only; NULL otherwise): every active expert
     // split into groups of at most kVirtTokens routed positions, in active order.
-    int4 *virt;       // [n_virt] {expert, first position, positions, cost weight before it}
-    int32_t *n_virt;  // [2] virtual experts, total cost weight
+    int4 *virt;       // [n_virt] {expert, first position, positions, token columns before it}
+    int32_t *n_virt;  // [2] virtual experts, token columns
     int32_t *vslot;   // [R] virtual expert of each routed position
 };
 
@@ -74,16 +73,17 @@ struct DecodeArgs {
     int R;           // T * k
     int nmax;        // upper bound on active experts: min(E, R)
     int n_virt_max;  // upper bound on virtual experts
-    // Per routed position: the outputs of each phase of the decode chain,
-    // contiguous in this order (zeroed by the decode kernel, then summed into).
-    float *t;   // [R][2r]  x.[A_g | A_u]
-    float *gu;  // [R][2f]  t_g.B_g | t_u.B_u
-    float *s;   // [R][r]   h.A_d, h = silu(t_g.B_g) * (t_u.B_u) [* w]
-    float *y;   // [R][d]   s.B_d (also the combine input of the prefill and EP paths)
-    // Decode stream: per-segment arrival counters of phases 1-4, and the count
-    // of CTAs that have zeroed their share of t..y.
-    uint32_t *arrive[4];
+    // Per-routed-row outputs s.B_d (the combine input of the prefill and EP paths).
+    float *y;   // [R][d]
+    // Decode chain: intermediates per virtual expert, [rows][token columns]
+    // fp32 (x0: gathered x, tb: x.[A_g | A_u], hb: silu(t_g.B_g) * (t_u.B_u)
+    // [* w], sb: h.A_d), and its counters (zeroed by the routing kernel): the
+    // item counter, the CTAs that zeroed their share of out, per phase and
+    // virtual expert the completed items.
+    float *x0, *tb, *hb, *sb;
+    uint32_t *queue;
     uint32_t *zero_done;
+    uint32_t *done;  // [5][n_virt_max]
 };
 
 int decode_sem_count(const DecodeArgs &a);

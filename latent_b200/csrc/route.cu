@@ -115,12 +115,14 @@ __device__ void block_stable_scatter(const int32_t *ids, int lo, int hi, int E, 
 
 // Virtual-expert table from counts/offsets/active (one block): per active
 // expert ceil(count / kVirtTokens) virtual experts, each with the prefix of
-// the cost weights before it.  nv and wv hold at least E ints of shared
-// scratch each; scratch as for block_exclusive_scan.
-__device__ void block_build_virt(const RouteArgs &a, int n_act, int *nv, int *wv, int *scratch) {
+// the token columns before it.  act/cnt/off are the active list, counts and
+// offsets (shared or global memory); nv and wv hold at least E ints of
+// shared scratch each; scratch as for block_exclusive_scan.
+__device__ void block_build_virt(const RouteArgs &a, int n_act, const int *act, const int *cnt, const int *off,
+                                 int *nv, int *wv, int *scratch) {
     const int tid = threadIdx.x;
     for (int i = tid; i < n_act; i += kRouteThreads) {
-        const int ne = a.counts[a.active[i]];
+        const int ne = cnt[act[i]];
         const int full = ne / kVirtTokens, rest = ne - full * kVirtTokens;
         nv[i] = full + (rest > 0);
         wv[i] = full * virt_weight(kVirtTokens) + (rest > 0 ? virt_weight(rest) : 0);
@@ -129,7 +131,7 @@ __device__ void block_build_virt(const RouteArgs &a, int n_act, int *nv, int *wv
     const int total = block_exclusive_scan(nv, n_act, scratch);
     const int wtotal = block_exclusive_scan(wv, n_act, scratch);
     for (int i = tid; i < n_act; i += kRouteThreads) {
-        const int e = a.active[i], ne = a.counts[e], p0 = a.offsets[e];
+        const int e = act[i], ne = cnt[e], p0 = off[e];
         int wsum = wv[i];
         for (int q = 0, v = nv[i]; q * kVirtTokens < ne; ++q, ++v) {
             const int first = p0 + q * kVirtTokens, n = min(kVirtTokens, ne - q * kVirtTokens);
@@ -148,9 +150,12 @@ __device__ void block_build_virt(const RouteArgs &a, int n_act, int *nv, int *wv
 // One block does everything (small R: decode).
 __global__ void __launch_bounds__(kRouteThreads) k_route_single(RouteArgs a) {
     extern __shared__ int sm[];
-    int *cnt = sm;                 // [E]
+    int *cnt = sm;                 // [E] counts, then running bases of the scatter
     int *scratch = cnt + a.E;      // [64]
     int *wcnt = scratch + 64;      // [32][E]
+    int *cnt_k = wcnt + 32 * a.E;  // [E] counts (kept)
+    int *off_k = cnt_k + a.E;      // [E] offsets (kept)
+    int *act = off_k + a.E;        // [E] active list
     const int tid = threadIdx.x;
     for (int i = tid; i < a.n_sem; i += kRouteThreads) a.sem[i] = 0;
     if (tid < 4) a.err[tid] = 0;
@@ -161,21 +166,29 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_single(RouteArgs a) {
         if (e >= 0 && e < a.E) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    for (int i = tid; i < a.E; i += kRouteThreads) a.counts[i] = cnt[i];
+    for (int i = tid; i < a.E; i += kRouteThreads) {
+        const int c = cnt[i];
+        cnt_k[i] = c;
+        a.counts[i] = c;
+        wcnt[i] = c > 0 ? 1 : 0;
+    }
     __syncthreads();
     const int total = block_exclusive_scan(cnt, a.E, scratch);
-    for (int i = tid; i < a.E; i += kRouteThreads) a.offsets[i] = cnt[i];
-    if (tid == 0) a.offsets[a.E] = total;
-    __syncthreads();
-    // active list: scan of (count > 0)
-    for (int i = tid; i < a.E; i += kRouteThreads) wcnt[i] = a.counts[i] > 0 ? 1 : 0;
-    __syncthreads();
     const int n_act = block_exclusive_scan(wcnt, a.E, scratch);
-    for (int i = tid; i < a.E; i += kRouteThreads)
-        if (a.counts[i] > 0) a.active[wcnt[i]] = i;
-    if (tid == 0) *a.n_active = n_act;
+    for (int i = tid; i < a.E; i += kRouteThreads) {
+        off_k[i] = cnt[i];
+        a.offsets[i] = cnt[i];
+        if (cnt_k[i] > 0) {
+            act[wcnt[i]] = i;
+            a.active[wcnt[i]] = i;
+        }
+    }
+    if (tid == 0) {
+        a.offsets[a.E] = total;
+        *a.n_active = n_act;
+    }
     __syncthreads();
-    if (a.virt) block_build_virt(a, n_act, wcnt, wcnt + a.E, scratch);
+    if (a.virt) block_build_virt(a, n_act, act, cnt_k, off_k, wcnt, wcnt + a.E, scratch);
     block_stable_scatter(a.ids, 0, a.R, a.E, a.top_k, cnt, wcnt, a.order, a.pos, a.err);
 }
 
@@ -231,7 +244,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_scan(RouteArgs a) {
         *a.n_active = n_act;
     }
     __syncthreads();
-    if (a.virt) block_build_virt(a, n_act, flag, cnt, scratch);
+    if (a.virt) block_build_virt(a, n_act, a.active, a.counts, a.offsets, flag, cnt, scratch);
 }
 
 // Pass 3: stable scatter within each block from its base offsets.
@@ -255,11 +268,12 @@ size_t route_block_counts_bytes(int E, int R) {
 
 cudaError_t launch_route(RouteArgs a, cudaStream_t s) {
     const size_t wsm = (size_t)(64 + (kRouteWarps + 1) * a.E) * sizeof(int);
-    cudaError_t err = ensure_smem((const void *)k_route_single, wsm);
+    const size_t ssm = wsm + (size_t)3 * a.E * sizeof(int);
+    cudaError_t err = ensure_smem((const void *)k_route_single, ssm);
     if (err == cudaSuccess) err = ensure_smem((const void *)k_route_scatter, wsm);
     if (err != cudaSuccess) return err;
     if (a.R <= kRouteSingleMax) {
-        k_route_single<<<1, kRouteThreads, wsm, s>>>(a);
+        k_route_single<<<1, kRouteThreads, ssm, s>>>(a);
         return cudaGetLastError();
     }
     a.chunk = kRouteChunk;
