@@ -1,6 +1,6 @@
 """The decode path at the benchmark's full size (config 1: 64 experts,
-d=2048, f=1408, r=256, top-6, 32 tokens, bf16 activations): a sample of tokens
-against the oracle, plus size-independent properties over the whole batch."""
+d=2048, f=1408, r=256, top-6, 32 tokens, bf16 activations): the whole batch
+against the oracle, plus size-independent properties."""
 
 import numpy as np
 import pytest
@@ -29,16 +29,15 @@ def _oracle_experts(es, experts):
     return out
 
 
-def test_token_sample_matches_oracle(c1):
+@pytest.mark.parametrize("wbd", [False, True])
+def test_whole_batch_matches_oracle(c1, wbd):
     cfg, es, x, ids, w = c1
-    y = ExpertFFN(es, path="decode")(x, ids, w).cpu().numpy()
-    sample = [0, 13, 31]
-    ids_s = ids[sample].cpu().numpy()
-    touched = sorted(set(ids_s.ravel().tolist()))
-    ex = _oracle_experts(es, touched)
+    y = ExpertFFN(es, path="decode")(x, ids, w, weight_before_down=wbd).cpu().numpy()
+    ids_np = ids.cpu().numpy()
+    ex = _oracle_experts(es, sorted(set(ids_np.ravel().tolist())))
     table = [ex.get(e) for e in range(cfg.n_expert)]
-    ref = O.moe_forward(x[sample].float().cpu().numpy(), ids_s, w[sample].cpu().numpy(), table)
-    assert rel(ref, y[sample]) <= TOL
+    ref = O.moe_forward(x.float().cpu().numpy(), ids_np, w.cpu().numpy(), table, weight_before_down=wbd)
+    assert rel(ref, y) <= TOL
 
 
 def test_weight_scaling_is_linear(c1):
