@@ -65,7 +65,7 @@ struct CUevent_st;  /* cudaEvent_t */
 #define LATENT_API
 #endif
 
-#define LATENT_ABI_VERSION 2
+#define LATENT_ABI_VERSION 3
 
 typedef enum latent_status {
     LATENT_OK = 0,
@@ -77,7 +77,8 @@ typedef enum latent_status {
     LATENT_ERR_WORKSPACE = 6,   /* workspace missing or too small */
     LATENT_ERR_TIMEOUT = 7,     /* a bounded device-side wait gave up */
     LATENT_ERR_CUDA = 8,        /* a CUDA runtime call failed */
-    LATENT_ERR_UNSUPPORTED = 9  /* valid request this build does not serve */
+    LATENT_ERR_UNSUPPORTED = 9, /* valid request this build does not serve */
+    LATENT_ERR_CAPACITY = 10    /* a fixed-capacity exchange block overflowed */
 } latent_status;
 
 typedef enum latent_type {
@@ -175,6 +176,10 @@ typedef struct latent_ep_desc {
 LATENT_API int latent_ep_workspace_size(const latent_ep_desc *desc, size_t *bytes);
 LATENT_API int latent_ep_dispatch(const latent_ep_desc *desc, struct CUstream_st *stream);
 LATENT_API int latent_ep_combine(const latent_ep_desc *desc, struct CUstream_st *stream);
+/* Synchronises `stream` and reports device-side errors recorded in the EP
+ * workspace since the last latent_ep_dispatch (LATENT_ERR_EXPERT_ID, and
+ * LATENT_ERR_CAPACITY from latent_ep_pack_fixed). */
+LATENT_API int latent_ep_check(const latent_ep_desc *desc, struct CUstream_st *stream);
 
 /* Fixed-capacity exchange blocks (no counterpart in the reference, which has
  * no multi-GPU code).  After latent_ep_dispatch on the same desc and
@@ -183,7 +188,9 @@ LATENT_API int latent_ep_combine(const latent_ep_desc *desc, struct CUstream_st 
  * [g*E/world, (g+1)*E/world); send_meta[world*cap][2] int32 holds
  * {global expert id, router weight bits} per row, {-1, 0} for unused rows.
  * cap must be at least the rows any destination receives (T*min(k, E/world)
- * when a token routes no expert twice).  latent_ep_combine_fixed reads the
+ * when a token routes no expert twice); a destination with more rows keeps
+ * its first cap and records LATENT_ERR_CAPACITY for latent_ep_check, and
+ * the rows left out contribute nothing to the combine.  latent_ep_combine_fixed reads the
  * returned blocks y_rows[world*cap][d] fp32 (same placement) and writes
  * out[T][d] = sum_j w[t,j] * y (plain sum with LATENT_FLAG_WEIGHT_BEFORE_DOWN).
  * Neither needs the host to know the per-destination counts. */
@@ -220,16 +227,23 @@ LATENT_API int latent_expert_ffn_forward(const latent_ffn_desc *desc, struct CUs
  * in the reference op.  It ignores desc->workspace and uses a 16 MiB scratch
  * array that the library keeps in device memory (reserved on every GPU that
  * loads the library, until exit); a call needing more returns
- * LATENT_ERR_WORKSPACE.  The first call on a device resolves the array's
- * address and should come before any stream capture.  All calls share the
- * array: calls that overlap on the GPU race.  Device-side errors of this
- * variant are not reported.  Allocates nothing. */
+ * LATENT_ERR_WORKSPACE.  The array's address is looked up on every call made
+ * outside stream capture; a captured call reuses the last one, so make one
+ * call on the device before capturing (else LATENT_ERR_UNSUPPORTED).  All
+ * calls share the array: calls that overlap on the GPU race.  Device-side
+ * errors are read with latent_expert_ffn_check_noalloc.  Allocates nothing. */
 LATENT_API int latent_expert_ffn_forward_noalloc(const latent_ffn_desc *desc, struct CUstream_st *stream);
+
+/* latent_expert_ffn_check for the scratch array of
+ * latent_expert_ffn_forward_noalloc on the current device (desc->workspace
+ * is ignored): synchronises `stream`, then reports the device-side errors
+ * the last no-alloc call recorded. */
+LATENT_API int latent_expert_ffn_check_noalloc(const latent_ffn_desc *desc, struct CUstream_st *stream);
 
 /* latent_expert_ffn_forward that also records the caller's events on
  * `stream` around each kernel it launches: events[0] before routing, then one
- * after routing and after every FFN kernel (decode: 4 phases + combine, so 7
- * events in all).  A profiling aid with no counterpart in the reference op;
+ * after routing and after every FFN kernel (decode: the routing kernel and
+ * the fused chain kernel, so 3 events in all).  A profiling aid with no counterpart in the reference op;
  * results are identical to latent_expert_ffn_forward. */
 LATENT_API int latent_expert_ffn_forward_timed(const latent_ffn_desc *desc, struct CUstream_st *stream,
                                                struct CUevent_st *const *events, int n_events);
@@ -237,6 +251,15 @@ LATENT_API int latent_expert_ffn_forward_timed(const latent_ffn_desc *desc, stru
 /* Synchronises `stream` and reports device-side errors recorded by the last
  * forward that used `workspace` (LATENT_ERR_EXPERT_ID, LATENT_ERR_TIMEOUT). */
 LATENT_API int latent_expert_ffn_check(const latent_ffn_desc *desc, struct CUstream_st *stream);
+
+/* Failure-path test hook, process-wide, for the decode path's fused kernel
+ * (no counterpart in the reference).  wait_ns (1 ms .. 2 s; 0 = the default
+ * 2 s) bounds every device-side wait of later launches; with
+ * unreachable_dependency != 0 each cross-CTA dependency wait also asks for
+ * one completion more than the kernel will ever make, so it runs out, the
+ * kernel records LATENT_ERR_TIMEOUT and unwinds without faulting, and the
+ * context stays usable.  Call (0, 0) to restore the defaults. */
+LATENT_API int latent_debug_set_wait_limit(uint64_t wait_ns, int32_t unreachable_dependency);
 
 /* Dequantize expert `expert` of one stacked factor to fp32 out[rows][cols],
  * bit-exact with dequantize_nf4 / dequantize_int8

@@ -18,7 +18,7 @@ LATENT_OK = 0
 STATUS_NAMES = {
     0: "LATENT_OK", 1: "LATENT_ERR_INVALID", 2: "LATENT_ERR_SHAPE", 3: "LATENT_ERR_DTYPE",
     4: "LATENT_ERR_ALIGN", 5: "LATENT_ERR_EXPERT_ID", 6: "LATENT_ERR_WORKSPACE",
-    7: "LATENT_ERR_TIMEOUT", 8: "LATENT_ERR_CUDA", 9: "LATENT_ERR_UNSUPPORTED",
+    7: "LATENT_ERR_TIMEOUT", 8: "LATENT_ERR_CUDA", 9: "LATENT_ERR_UNSUPPORTED", 10: "LATENT_ERR_CAPACITY",
 }
 
 TYPE_F32, TYPE_F16, TYPE_BF16 = 0, 1, 2
@@ -97,12 +97,15 @@ EXPORTS.update({
     "latent_ep_workspace_size": (C.c_int, [C.POINTER(EpDesc), C.POINTER(C.c_size_t)]),
     "latent_ep_dispatch": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_ep_combine": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
+    "latent_ep_check": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_abi_version": (C.c_int, []),
     "latent_status_string": (C.c_char_p, [C.c_int]),
     "latent_expert_ffn_workspace_size": (C.c_int, [C.POINTER(FfnDesc), C.POINTER(C.c_size_t)]),
     "latent_expert_ffn_forward": (C.c_int, [C.POINTER(FfnDesc), C.c_void_p]),
     "latent_expert_ffn_check": (C.c_int, [C.POINTER(FfnDesc), C.c_void_p]),
     "latent_expert_ffn_forward_noalloc": (C.c_int, [C.POINTER(FfnDesc), C.c_void_p]),
+    "latent_expert_ffn_check_noalloc": (C.c_int, [C.POINTER(FfnDesc), C.c_void_p]),
+    "latent_debug_set_wait_limit": (C.c_int, [C.c_uint64, C.c_int32]),
     "latent_expert_ffn_forward_timed": (C.c_int, [C.POINTER(FfnDesc), C.c_void_p, C.POINTER(C.c_void_p), C.c_int]),
     "latent_dequantize": (C.c_int, [C.POINTER(QMatrix), C.c_int32, C.c_void_p, C.c_void_p]),
     "latent_silu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),
@@ -140,7 +143,7 @@ def lib() -> C.CDLL:
                 fn = getattr(h, name)
                 fn.restype = res
                 fn.argtypes = args
-            if h.latent_abi_version() != 2:
+            if h.latent_abi_version() != 3:
                 raise RuntimeError("liblatent_b200.so ABI version mismatch")
             _lib = h
     return _lib

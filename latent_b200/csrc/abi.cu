@@ -166,6 +166,7 @@ extern "C" LATENT_API const char *latent_status_string(int status) {
         case LATENT_ERR_TIMEOUT: return "bounded device wait timed out";
         case LATENT_ERR_CUDA: return "CUDA runtime error";
         case LATENT_ERR_UNSUPPORTED: return "request not supported by this build";
+        case LATENT_ERR_CAPACITY: return "a fixed-capacity exchange block overflowed";
         default: return "unknown status";
     }
 }
@@ -383,6 +384,7 @@ EpArgs ep_args(const latent_ep_desc *d) {
     e.send_x = d->send_x;
     e.send_expert = d->send_expert;
     e.send_weight = d->send_weight;
+    e.err = at<uint32_t>(d->workspace, L.err);
     return e;
 }
 
@@ -414,6 +416,21 @@ extern "C" LATENT_API int latent_ep_combine_fixed(const latent_ep_desc *desc, in
     return cuda_status(launch_ep_combine_fixed(ep_args(desc), at<int32_t>(desc->workspace, L.pos), world, cap, y_rows,
                                                out, (desc->flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN) != 0,
                                                reinterpret_cast<cudaStream_t>(stream)));
+}
+
+extern "C" LATENT_API int latent_ep_check(const latent_ep_desc *desc, CUstream_st *stream) {
+    int st = ep_validate(desc);
+    if (st) return st;
+    if (desc->n_tokens == 0) return LATENT_OK;
+    if (!desc->workspace || desc->workspace_bytes < ep_layout(desc).total) return LATENT_ERR_WORKSPACE;
+    if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return LATENT_ERR_CUDA;
+    uint32_t err = 0;
+    if (cudaMemcpy(&err, at<uint32_t>(desc->workspace, ep_layout(desc).err), sizeof(err), cudaMemcpyDeviceToHost) !=
+        cudaSuccess)
+        return LATENT_ERR_CUDA;
+    if (err & kErrExpertId) return LATENT_ERR_EXPERT_ID;
+    if (err & kErrCapacity) return LATENT_ERR_CAPACITY;
+    return LATENT_OK;
 }
 
 extern "C" LATENT_API int latent_ep_combine(const latent_ep_desc *desc, CUstream_st *stream) {

@@ -58,6 +58,7 @@
 #include <cuda.h>
 #include <string.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 
@@ -92,7 +93,8 @@ static_assert(kOffHdr % 16 == 0, "slot alignment");
 // Dynamic shared memory: region A (barriers, INT8 row lists, cross-warp
 // buffer, slot 0) below shared address 64 K, the lookup table at
 // [64 K, 128 K), slots 1.. above it.
-constexpr int kBarBytes = 256;                        // mbarriers: full, empty, hdr per slot
+constexpr int kBarBytes = 256;                        // mbarriers: full, empty, hdr per slot; consumers
+static_assert(8 * (3 * kSlots + 1) <= kBarBytes, "mbarrier area");
 constexpr int kListBytes = kNW * kStageRows * 4;      // per-warp INT8 row lists
 constexpr int kPreBytes = kNW * 64;                   // per-warp slots and router weights of the current item
 constexpr int kXbufBytes = 2 * kNW * 32 * 8 * 4;      // [matrix][warp][lane][8] cross-warp partial sums
@@ -138,6 +140,8 @@ struct Args {
     float *tb, *hb, *sb;    // intermediates [token columns][rows] of 2r, f, r
     int chunk1, chunk3;     // K-chunk rows of P1 (over d) and P3 (over f)
     uint32_t tma_mask;      // bit i: maps.m[i] is valid (codes of mat[i] as [rows of 128 B])
+    unsigned long long wait_ns;  // limit of every bounded wait (kWaitNs unless a test shortens it)
+    uint32_t dep_extra;          // test hook: completions each dependency wait wants beyond the real count
 };
 
 // TMA maps of the factors' codes viewed as rows of 128 bytes (one full
@@ -193,7 +197,7 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 }
 // Bounded wait for phase `parity` of the barrier; false once the wait gave up
 // (kErrTimeout recorded) or another wait already did.
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t *err) {
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t *err, unsigned long long limit) {
     unsigned long long t0 = 0;
     for (unsigned i = 0;; ++i) {
         uint32_t done;
@@ -210,7 +214,7 @@ __device__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t *err) {
             const unsigned long long now = gtime();
             if (i == 0) {
                 t0 = now;
-            } else if (now - t0 > kWaitNs) {
+            } else if (now - t0 > limit) {
                 atomicOr(err, kErrTimeout);
                 return false;
             }
@@ -302,9 +306,6 @@ __device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
 __device__ __forceinline__ void sts_f4(uint32_t addr, float4 v) {
     asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                  : "memory");
-}
-__device__ __forceinline__ void named_sync_consumers() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kNW * 32) : "memory");
 }
 
 // --- item geometry ---------------------------------------------------------------
@@ -568,7 +569,7 @@ __device__ void producer_run(const Args &a, const CodeMaps &maps, const Geo &g, 
         const int r_rows = a.r;
         for (int s = 0; s < cur.n_stages; ++s) {
             const uint32_t full = full0 + 8 * slot, empty = empty0 + 8 * slot, hdrb = hdr0 + 8 * slot;
-            if (lane == 0) ok = mbar_wait(empty, (empty_par >> slot) & 1u, a.err);
+            if (lane == 0) ok = mbar_wait(empty, (empty_par >> slot) & 1u, a.err, a.wait_ns);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             const uint32_t sbase = smem_u32(slot_ptr[slot]);
@@ -647,7 +648,7 @@ __device__ void producer_run(const Args &a, const CodeMaps &maps, const Geo &g, 
         have_nxt = have_nn;
     }
     if (lane == 0) {
-        if (ok && mbar_wait(empty0 + 8 * slot, (empty_par >> slot) & 1u, a.err)) {
+        if (ok && mbar_wait(empty0 + 8 * slot, (empty_par >> slot) & 1u, a.err, a.wait_ns)) {
             reinterpret_cast<Hdr *>(slot_ptr[slot] + kOffHdr)->kind = kStop;
             mbar_arrive(full0 + 8 * slot);
             mbar_arrive(hdr0 + 8 * slot);
@@ -711,7 +712,7 @@ __device__ void input_run(const Args &a, const Geo &g, const Slots &slot_ptr, ui
     for (int t = 0; t < 8; ++t) tok[t] = -1;
     while (true) {
         bool ok = true;
-        if (lane == 0) ok = mbar_wait(hdr0 + 8 * slot, (par >> slot) & 1u, a.err);
+        if (lane == 0) ok = mbar_wait(hdr0 + 8 * slot, (par >> slot) & 1u, a.err, a.wait_ns);
         if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) return;
         par ^= 1u << slot;
         const uint8_t *sp = slot_ptr[slot];
@@ -739,13 +740,13 @@ __device__ void input_run(const Args &a, const Geo &g, const Slots &slot_ptr, ui
             if (lane == 0) mbar_arrive(full);
         } else if (lane == 0) {
             const uint32_t *dep = a.done + (int64_t)(h.kind - 1) * a.n_virt_max + h.v;
-            const uint32_t target = (uint32_t)(kNW * g.per_v[h.kind - 1]);
+            const uint32_t target = (uint32_t)(kNW * g.per_v[h.kind - 1]) + a.dep_extra;
             if (!(dep == ok_ptr && target <= ok_target)) {
                 const unsigned long long t0 = gtime();
                 unsigned ns = 32;
                 while (ld_acquire(dep) < target) {
                     if (aborted(a.err)) break;
-                    if (gtime() - t0 > kWaitNs) {
+                    if (gtime() - t0 > a.wait_ns) {
                         atomicOr(a.err, kErrTimeout);
                         break;
                     }
@@ -783,7 +784,20 @@ struct Warp {
     int *pre;         // [8] slots, [8] router weights (float bits) of the current item's tokens
     bool zeroed;      // the kernel-start zeroing is known complete
     int pend_kind, pend_v;  // completion count not yet released
+    uint32_t xbar, xpar;    // the consumer warps' barrier and the phase this warp waits for next
 };
+
+// Bounded barrier of the kNW consumer warps (an mbarrier taking one arrival
+// per warp; arrive releases, try_wait acquires).  False once the wait gave
+// up: the warp then unwinds.  A bar.sync would wait forever for a consumer
+// warp that had already unwound after an expired wait.
+__device__ __forceinline__ bool consumers_sync(const Args &a, Warp &wc) {
+    __syncwarp();
+    if (wc.lane == 0) mbar_arrive(wc.xbar);
+    const bool ok = mbar_wait(wc.xbar, wc.xpar, a.err, a.wait_ns);
+    wc.xpar ^= 1u;
+    return __all_sync(0xffffffffu, ok);
+}
 
 // Main loop over the warp's rows of one stage, then the stage's INT8 rows.
 template <int NT>
@@ -946,7 +960,7 @@ __device__ void wait_zeroed(const Args &a) {
     const unsigned long long t0 = gtime();
     while (ld_acquire(a.zero_done) < gridDim.x) {
         if (aborted(a.err)) return;
-        if (gtime() - t0 > kWaitNs) {
+        if (gtime() - t0 > a.wait_ns) {
             atomicOr(a.err, kErrTimeout);
             return;
         }
@@ -1041,7 +1055,7 @@ __device__ void consumer_run(const Args &a, const Slots &slot_ptr, uint32_t bars
         const uint32_t par = (par_bits >> slot) & 1u;
         // a pending completion must not wait behind a stage that may depend on it
         if (wc.pend_kind >= 0 && !mbar_test(full, par)) release_pending(a, wc);
-        if (!mbar_wait(full, par, a.err)) return;
+        if (!__all_sync(0xffffffffu, mbar_wait(full, par, a.err, a.wait_ns))) return;
         par_bits ^= 1u << slot;
         const uint8_t *sp = slot_ptr[slot];
         const uint32_t sb = smem_u32(sp);
@@ -1107,7 +1121,7 @@ __device__ void consumer_run(const Args &a, const Slots &slot_ptr, uint32_t bars
                     d1[t] = uv[t];
                 }
             }
-            named_sync_consumers();
+            if (!consumers_sync(a, wc)) return;
             if (g >= 0 && rp == 0) {
                 for (int q = 1; q < P; ++q) {
                     const int ow = q * h.ng + g;
@@ -1120,7 +1134,7 @@ __device__ void consumer_run(const Args &a, const Slots &slot_ptr, uint32_t bars
                     }
                 }
             }
-            named_sync_consumers();  // the buffer is rewritten by the next narrow item
+            if (!consumers_sync(a, wc)) return;  // the buffer is rewritten by the next narrow item
         }
         if (h.kind != 2 && !wc.zeroed) {  // red.add targets are zeroed by every CTA at kernel start
             if (lane == 0) wait_zeroed(a);
@@ -1165,13 +1179,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(Args args, const __grid_c
     }
     slot_ptr.s1 = dsm + (kTableAddr + kTableBytes - a0);
     uint8_t *table = dsm + (kTableAddr - a0);
-    const uint32_t bars = smem_u32(ctl);  // full[kSlots], empty[kSlots], hdr[kSlots]
+    const uint32_t bars = smem_u32(ctl);  // full[kSlots], empty[kSlots], hdr[kSlots], consumer barrier
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(bars + 8 * s, 2);                 // producer + input warp (+ transaction bytes)
             mbar_init(bars + 8 * (kSlots + s), kNW);    // consumer warps
             mbar_init(bars + 8 * (2 * kSlots + s), 1);  // producer
         }
+        mbar_init(bars + 8 * 3 * kSlots, kNW);  // the consumer warps' barrier
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();  // sargs and the barriers
@@ -1228,6 +1243,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(Args args, const __grid_c
         wc.zeroed = false;
         wc.pend_kind = -1;
         wc.pend_v = 0;
+        wc.xbar = bars + 8 * 3 * kSlots;
+        wc.xpar = 0;
         consumer_run(a, slot_ptr, bars, wc);
     }
 }
@@ -1342,6 +1359,10 @@ bool codes_map(CUtensorMap *out, const latent_qmatrix &m, int E) {
 
 }  // namespace
 
+// Failure-path test hook (latent_debug_set_wait_limit).
+std::atomic<unsigned long long> g_wait_ns{kWaitNs};
+std::atomic<uint32_t> g_dep_extra{0};
+
 cudaError_t launch_decode(const DecodeArgs &d, cudaStream_t s, Marks *marks) {
     const void *fn = (const void *)k_chain;
     int dev = 0;
@@ -1399,6 +1420,8 @@ cudaError_t launch_decode(const DecodeArgs &d, cudaStream_t s, Marks *marks) {
     a.sb = d.sb;
     a.chunk1 = chunk_rows(d.d, d.r < 256 ? d.r : 256);
     a.chunk3 = chunk_rows(d.f, d.r < 256 ? d.r : 256);
+    a.wait_ns = g_wait_ns.load();
+    a.dep_extra = g_dep_extra.load();
     CodeMaps maps;
     memset(&maps, 0, sizeof(maps));
     a.tma_mask = 0;
@@ -1411,3 +1434,10 @@ cudaError_t launch_decode(const DecodeArgs &d, cudaStream_t s, Marks *marks) {
 }
 
 }  // namespace latent
+
+extern "C" LATENT_API int latent_debug_set_wait_limit(uint64_t wait_ns, int32_t unreachable_dependency) {
+    if (wait_ns != 0 && (wait_ns < 1000000ull || wait_ns > latent::kWaitNs)) return LATENT_ERR_INVALID;
+    latent::g_wait_ns.store(wait_ns ? wait_ns : latent::kWaitNs);
+    latent::g_dep_extra.store(unreachable_dependency ? 1u : 0u);
+    return LATENT_OK;
+}

@@ -15,6 +15,7 @@ enum : uint32_t {
     kErrExpertId = 1u << 0,
     kErrTimeout = 1u << 1,
     kErrLayout = 1u << 2,  // a kernel's shared-memory layout assumption did not hold
+    kErrCapacity = 1u << 3,  // a fixed-capacity exchange block had more rows than it holds
 };
 
 // NF4 levels in code order.  Must equal the reference table

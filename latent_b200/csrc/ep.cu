@@ -32,13 +32,17 @@ __global__ void __launch_bounds__(128) k_ep_gather(EpArgs a) {
 
 // Fixed-capacity block q of the send buffer: block g = q / cap holds the
 // rows routed to rank g's experts [g*el, (g+1)*el) in routed order, rows past
-// their count get expert id -1.  One block per padded row.
+// their count get expert id -1.  One block per padded row.  A destination
+// with more rows than cap (only possible when a token routes one expert
+// twice) keeps its first cap rows and sets kErrCapacity.
 template <int XT>
 __global__ void __launch_bounds__(128) k_ep_pack_fixed(EpArgs a, int el, int cap, void *rows, int32_t *meta) {
     const int q = blockIdx.x;
     const int g = q / cap, i = q - g * cap;
     const int p = a.offsets[g * el] + i;
-    const bool valid = p < a.offsets[(g + 1) * el];
+    const int end = a.offsets[(g + 1) * el];
+    const bool valid = p < end;
+    if (threadIdx.x == 0 && i == 0 && end - p > cap) atomicOr(a.err, kErrCapacity);
     if (threadIdx.x == 0) {
         meta[2 * q] = valid ? a.send_expert[p] : -1;
         meta[2 * q + 1] = valid ? __float_as_int(a.send_weight[p]) : 0;

@@ -125,6 +125,7 @@ struct EpArgs {
     void *send_x;
     int32_t *send_expert;
     float *send_weight;
+    uint32_t *err;           // workspace error word (kErrCapacity)
 };
 
 cudaError_t launch_ep_gather(const EpArgs &a, cudaStream_t s);

@@ -23,12 +23,14 @@
 //   calls queued one after another on a stream are independent.  Calls
 //   that overlap on the GPU (two streams, two host threads without ordering)
 //   race on the array and give undefined results.
-// * The first call on each device, with that device current, resolves the
-//   array's device address (cudaGetSymbolAddress); make that first call
-//   before any stream capture.
-// * Device-side errors of this variant (a routed id >= n_expert) are
-//   recorded in the internal array and are not reported;
-//   latent_expert_ffn_check() needs a caller-owned workspace.
+// * The array's device address is looked up (cudaGetSymbolAddress) on every
+//   call made outside stream capture, so a device reset or a new context is
+//   picked up; a call made while `stream` is capturing reuses the address of
+//   the last uncaptured call on that device, so make one call on each device
+//   before capturing (a capture cannot span a device reset).
+// * Device-side errors (a routed id >= n_expert, an expired wait) are
+//   recorded in the array's error word; read them with
+//   latent_expert_ffn_check_noalloc().
 // Nothing here calls cudaMalloc, cudaFree or any allocating routine.
 #include <mutex>
 
@@ -45,16 +47,21 @@ __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 std::mutex g_mu;
 void *g_ptr[kMaxDevices] = {};
 
-// Device address of g_static_scratch on the current device (set up once per device).
-int static_scratch(void **out) {
+// Device address of g_static_scratch on the current device: looked up afresh
+// unless `stream` is capturing, when the last looked-up address is used.
+int static_scratch(cudaStream_t stream, void **out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return LATENT_ERR_CUDA;
     if (dev < 0 || dev >= kMaxDevices) return LATENT_ERR_UNSUPPORTED;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) return LATENT_ERR_CUDA;
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_ptr[dev]) {
+    if (cap == cudaStreamCaptureStatusNone) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) return LATENT_ERR_CUDA;
         g_ptr[dev] = p;
+    } else if (!g_ptr[dev]) {
+        return LATENT_ERR_UNSUPPORTED;  // first call on this device is inside a capture
     }
     *out = g_ptr[dev];
     return LATENT_OK;
@@ -71,9 +78,20 @@ extern "C" LATENT_API int latent_expert_ffn_forward_noalloc(const latent_ffn_des
     if (need > latent::kStaticScratchBytes) return LATENT_ERR_WORKSPACE;
     if (desc->n_tokens == 0) return latent_expert_ffn_forward(desc, stream);
     void *scratch = nullptr;
-    if ((st = latent::static_scratch(&scratch))) return st;
+    if ((st = latent::static_scratch(reinterpret_cast<cudaStream_t>(stream), &scratch))) return st;
     latent_ffn_desc local = *desc;
     local.workspace = scratch;
     local.workspace_bytes = latent::kStaticScratchBytes;
     return latent_expert_ffn_forward(&local, stream);
+}
+
+extern "C" LATENT_API int latent_expert_ffn_check_noalloc(const latent_ffn_desc *desc, CUstream_st *stream) {
+    if (!desc) return LATENT_ERR_INVALID;
+    void *scratch = nullptr;
+    int st = latent::static_scratch(reinterpret_cast<cudaStream_t>(stream), &scratch);
+    if (st) return st;
+    latent_ffn_desc local = *desc;
+    local.workspace = scratch;
+    local.workspace_bytes = latent::kStaticScratchBytes;
+    return latent_expert_ffn_check(&local, stream);
 }

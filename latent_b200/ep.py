@@ -41,6 +41,7 @@ class Packed:
     send_weight: torch.Tensor   # [T*k] float32
     expert_counts: torch.Tensor  # [E] int32
     state: object = None         # whatever combine needs
+    overflow: bool = False       # a fixed-capacity block overflowed (host-side packing only)
 
 
 class CudaEPOps:
@@ -104,6 +105,13 @@ class CudaEPOps:
                                                       _stream_ptr(x.device)), "latent_ep_combine_fixed")
         return out
 
+    def check(self, p: Packed) -> None:
+        """Synchronise and raise on device-side errors of this dispatch (an
+        expert id out of range, a fixed-capacity block that overflowed)."""
+        x, ids, weights, wbd = p.state
+        d = self._desc(x, ids, weights, wbd)
+        _lib.check(_lib.lib().latent_ep_check(C.byref(d), _stream_ptr(x.device)), "latent_ep_check")
+
     def combine(self, p: Packed, y_back: torch.Tensor) -> torch.Tensor:
         x, ids, weights, wbd = p.state
         out = torch.empty((ids.shape[0], x.shape[1]), dtype=torch.float32, device=x.device)
@@ -125,7 +133,10 @@ class ExpertParallelFFN:
         (a token routes at most that many slots to one rank); rows past a
         destination's count carry expert id -1, which the fused op skips.
         The whole call is stream-ordered, so consecutive calls pipeline and
-        the call can be captured with its collectives.
+        the call can be captured with its collectives.  A batch in which a
+        token routes one expert twice can overflow a block: its extra rows
+        are left out of the exchange and the combine, and ``check()`` (a
+        host synchronisation) raises LATENT_ERR_CAPACITY.
     """
 
     def __init__(self, n_expert: int, ops, group=None, max_tokens: Optional[int] = None):
@@ -136,6 +147,12 @@ class ExpertParallelFFN:
             raise ValueError(f"{n_expert} experts do not split evenly over {self.world} ranks")
         if max_tokens is not None and max_tokens < 1:
             raise ValueError(f"max_tokens must be positive, got {max_tokens}")
+        # Every rank must size the fixed blocks alike, or the all-to-alls
+        # disagree on their splits: compare once, here, on the host.
+        seen = [None] * self.world
+        dist.all_gather_object(seen, max_tokens, group=group)
+        if any(m != max_tokens for m in seen):
+            raise ValueError(f"max_tokens differs across ranks: {seen}")
         self.n_expert = n_expert
         self.e_local = n_expert // self.world
         self.base = self.rank * self.e_local
@@ -143,6 +160,15 @@ class ExpertParallelFFN:
         self.max_tokens = max_tokens
         self._counts = None
         self._pos = None
+        self._last = None
+
+    def check(self) -> None:
+        """Synchronise and raise if the last call recorded a device-side error
+        (an expert id out of range, or a fixed-capacity block overflow)."""
+        if self._last is not None and hasattr(self.ops, "check"):
+            self.ops.check(self._last)
+        elif self._last is not None and getattr(self._last, "overflow", False):
+            raise _lib.LatentError(10, "fixed-capacity exchange")
 
     @property
     def last_counts(self):
@@ -168,6 +194,7 @@ class ExpertParallelFFN:
         both = torch.stack([send_counts, recv_counts]).cpu()
         sc, rc = both[0].tolist(), both[1].tolist()
         self._counts = (sc, rc)
+        self._last = p
         n_send, n_recv = sum(sc), sum(rc)
         recv_x = torch.empty((n_recv, d), dtype=x.dtype, device=x.device)
         dist.all_to_all_single(recv_x, p.send_x[:n_send].contiguous(), rc, sc, group=self.group)
@@ -218,9 +245,12 @@ class ExpertParallelFFN:
         y_pad = torch.empty((G * cap, d), dtype=torch.float32, device=dev)
         dist.all_to_all_single(y_pad, y.contiguous(), group=self.group)
         self._counts = (send_counts, (rid.view(G, cap) >= 0).sum(dim=1))
+        self._last = p
         if fused:
             return self.ops.combine_fixed(p, y_pad, G, cap)
-        return self.ops.combine(p, y_pad.index_select(0, dst.clamp(max=G * cap - 1)))
+        # rows that did not fit their block (dst = G*cap) read a zero row
+        y_ext = torch.cat([y_pad, y_pad.new_zeros((1, d))])
+        return self.ops.combine(p, y_ext.index_select(0, dst))
 
     def _fixed_rows(self, p, send_counts, G: int, cap: int) -> torch.Tensor:
         """Block row of every routed position (G*cap past the routed rows: a discard row)."""
@@ -233,4 +263,6 @@ class ExpertParallelFFN:
         g = torch.searchsorted(end, pos, right=True)
         gc = g.clamp(max=G - 1)
         slot = pos - (end - send_counts)[gc]
-        return torch.where(g < G, gc * cap + slot, torch.full_like(pos, G * cap))
+        keep = (g < G) & (slot < cap)
+        p.overflow = bool((send_counts > cap).any())
+        return torch.where(keep, gc * cap + slot, torch.full_like(pos, G * cap))

@@ -244,7 +244,8 @@ class ExpertFFN:
         return out
 
     def check(self) -> None:
-        """Synchronises and raises if the last call routed an expert id >= n_expert."""
+        """Synchronises and raises if the last call recorded a device-side error
+        (an expert id >= n_expert was routed, or a bounded wait ran out)."""
         if self._last_desc is not None:
             _lib.check(_lib.lib().latent_expert_ffn_check(C.byref(self._last_desc),
                                                           _stream_ptr(self.experts.device)), "device check")

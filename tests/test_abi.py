@@ -32,8 +32,15 @@ def test_exports_match_header(lib):
         assert hasattr(lib, name), name
 
 
+def test_wait_limit_hook_validates_on_the_host(lib):
+    assert lib.latent_debug_set_wait_limit(10, 0) == 1             # below 1 ms
+    assert lib.latent_debug_set_wait_limit(10 ** 12, 0) == 1       # above the 2 s default
+    assert lib.latent_debug_set_wait_limit(50_000_000, 1) == 0
+    assert lib.latent_debug_set_wait_limit(0, 0) == 0               # defaults back
+
+
 def test_version_and_status_strings(lib):
-    assert lib.latent_abi_version() == 2
+    assert lib.latent_abi_version() == 3
     assert lib.latent_status_string(0) == b"ok"
     assert b"expert id" in lib.latent_status_string(5)
 

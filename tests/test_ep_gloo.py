@@ -134,3 +134,114 @@ def test_ep_fixed_capacity_rejects_larger_batch():
                            start_method="spawn")
         for r in range(world):
             assert "max_tokens" in (Path(tmp) / f"r{r}.txt").read_text()
+
+
+# ---- failure paths: made on the host, never on a device -------------------
+
+def _run_ranks(fn, world, tmp, deadline=90.0):
+    """Start `world` spawned ranks running fn(rank, world, port, tmp);
+    fail (after killing them) if they have not all ended within `deadline` s."""
+    import time
+    tmp = str(tmp)
+    ctx = mp.start_processes(fn, args=(world, _free_port(), tmp), nprocs=world, join=False,
+                             start_method="spawn")
+    end = time.monotonic() + deadline
+    try:
+        while not ctx.join(timeout=1.0):
+            if time.monotonic() > end:
+                pytest.fail(f"ranks still running after {deadline} s")
+    finally:
+        for p in ctx.processes:
+            if p.is_alive():
+                p.kill()
+    return tmp
+
+
+def _rank_leaves(rank, world, port, outdir):
+    """Rank 1 leaves between steps (after the first call); rank 0 makes a
+    second call, whose first collective must end in an error, not a hang."""
+    import datetime
+    sys.path.insert(0, str(ROOT))
+    from latent_b200.ep import ExpertParallelFFN
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    E, d, f, r, k = 4, 64, 96, 32, 2
+    ops = CpuEPOps(_table(E, d, f, r), E, base=rank * (E // world))
+    ep = ExpertParallelFFN(E, ops)
+    x = torch.randn((6, d))
+    ids = torch.randint(0, E, (6, k), dtype=torch.int32)
+    w = torch.rand((6, k))
+    ep(x, ids, w)                                     # step 1: both ranks
+    if rank == 1:
+        (Path(outdir) / "r1.txt").write_text("left")
+        os._exit(0)                                   # leaves without a word to the others
+    try:
+        ep(x, ids, w)                                 # step 2: rank 1 is gone
+        msg = "no error"
+    except Exception as e:                            # gloo: connection closed or timed out
+        msg = "raised " + type(e).__name__
+    (Path(outdir) / "r0.txt").write_text(msg)
+    os._exit(0)
+
+
+def test_ep_rank_that_leaves_ends_the_next_collective_with_an_error(tmp_path):
+    tmp = _run_ranks(_rank_leaves, 2, tmp_path)
+    assert (Path(tmp) / "r1.txt").read_text() == "left"
+    assert (Path(tmp) / "r0.txt").read_text().startswith("raised")
+
+
+def _mismatched_caps(rank, world, port, outdir):
+    sys.path.insert(0, str(ROOT))
+    from latent_b200.ep import ExpertParallelFFN
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ExpertParallelFFN(4, None, max_tokens=8 + 4 * rank)
+        msg = "no error"
+    except ValueError as e:
+        msg = str(e)
+    (Path(outdir) / f"r{rank}.txt").write_text(msg)
+    dist.destroy_process_group()
+
+
+def test_ep_fixed_capacity_mismatch_across_ranks_is_rejected_on_every_rank(tmp_path):
+    tmp = _run_ranks(_mismatched_caps, 2, tmp_path)
+    for r in range(2):
+        assert "differs across ranks" in (Path(tmp) / f"r{r}.txt").read_text()
+
+
+def _repeated_ids(rank, world, port, outdir):
+    """Tokens that route one expert twice overflow the fixed blocks (cap =
+    M * min(k, E/G) assumes distinct experts per token): with E=2 over 2
+    ranks and k=2, cap = M, and T tokens that all route expert 0 twice send
+    2T rows to rank 0.  The block keeps the first T rows in routed order (the
+    first T/2 tokens, both slots); the rest are left out of the exchange and
+    the combine, and check() reports the overflow."""
+    sys.path.insert(0, str(ROOT))
+    import oracle as O
+    from latent_b200 import _lib
+    from latent_b200.ep import ExpertParallelFFN
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    E, d, f, r, k, T = 2, 64, 96, 32, 2, 4
+    table = _table(E, d, f, r)
+    ep = ExpertParallelFFN(E, CpuEPOps(table, E, base=rank), max_tokens=T)
+    x = torch.randn((T, d), generator=torch.Generator().manual_seed(rank))
+    ids = torch.zeros((T, k), dtype=torch.int32)
+    w = torch.full((T, k), 0.5)
+    out = ep(x, ids, w).numpy()
+    ref = O.moe_forward(x.numpy(), ids.numpy(), w.numpy(), table)
+    kept = O.rel_l2(ref[:T // 2], out[:T // 2]) < 1e-6 and not out[T // 2:].any()
+    try:
+        ep.check()
+        msg = "no error"
+    except _lib.LatentError as e:
+        msg = f"status {e.status}"
+    (Path(outdir) / f"r{rank}.txt").write_text(f"{kept} {msg}")
+    dist.destroy_process_group()
+
+
+def test_ep_fixed_capacity_overflow_is_dropped_and_reported(tmp_path):
+    tmp = _run_ranks(_repeated_ids, 2, tmp_path)
+    for r in range(2):
+        assert (Path(tmp) / f"r{r}.txt").read_text() == "True status 10"

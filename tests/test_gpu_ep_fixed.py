@@ -47,3 +47,37 @@ def test_pack_and_combine_fixed_match_exact_splits(cuda, wbd):
     want = ops.combine(p, y_back)
     got = ops.combine_fixed(p, y_rows, world, cap)
     assert torch.equal(got, want)
+
+
+def test_pack_fixed_overflow_keeps_the_first_rows_and_is_reported(cuda):
+    """A token that routes one expert twice can overflow its block (cap
+    assumes distinct experts per token): the block keeps its first cap rows
+    in routed order, the rest are left out of the combine, and
+    latent_ep_check reports LATENT_ERR_CAPACITY.  The next clean dispatch
+    clears it."""
+    from latent_b200 import _lib
+    dev = torch.device("cuda", 0)
+    cfg = synth.CONFIGS[0]
+    E, world, T, k = cfg.n_expert, 8, 6, 2
+    es = ExpertSet(synth.make_expert_factors(cfg, dev, experts=[0]), device=dev, rank=cfg.rank)
+    x, _, _ = synth.make_batch(cfg, dev, n_tokens=T)
+    ids = torch.zeros((T, k), dtype=torch.int32, device=dev)      # 2T rows to rank 0
+    w = torch.full((T, k), 0.5, device=dev)
+    cap = T * min(k, E // world)                                    # = T
+    ops = CudaEPOps(es, E)
+    p = ops.dispatch(x, ids, w, False)
+    rows, meta = ops.pack_fixed(p, world, cap)
+    with pytest.raises(_lib.LatentError) as info:
+        ops.check(p)
+    assert info.value.status == 10                                  # LATENT_ERR_CAPACITY
+    assert torch.equal(rows[:cap].cpu(), p.send_x[:cap].cpu())
+    assert (meta[:cap, 0] == 0).all() and (meta[cap:, 0] == -1).all()
+    y_rows = torch.randn((world * cap, cfg.n_embd), device=dev)
+    got = ops.combine_fixed(p, y_rows, world, cap)
+    # the exact-split combine over send order, with the rows past cap zero
+    y_back = torch.zeros((T * k, cfg.n_embd), device=dev)
+    y_back[:cap] = y_rows[:cap]
+    assert torch.equal(got, ops.combine(p, y_back))
+    ok = ops.dispatch(x, torch.stack([ids[:, 0], ids[:, 0] + 1], dim=1).contiguous(), w, False)
+    ops.pack_fixed(ok, world, cap)
+    ops.check(ok)

@@ -57,6 +57,29 @@ def test_noalloc_matches_regular_entry_on_consecutive_calls(cuda, layer):
         assert O.rel_l2(ref.cpu().numpy(), got.cpu().numpy()) <= TOL
 
 
+def test_noalloc_reports_device_errors(cuda):
+    """A routed id past n_expert is skipped and recorded in the scratch's
+    error word; latent_expert_ffn_check_noalloc reads it, and the next clean
+    call clears it."""
+    z = golden("moe")
+    facs, _ = golden_moe_experts(z)
+    es = ExpertSet(facs, device="cuda")
+    op = ExpertFFN(es, path="decode")
+    x = torch.from_numpy(z["x"]).cuda()
+    ids = torch.from_numpy(z["ids"]).cuda()
+    w = torch.from_numpy(z["weights"]).cuda()
+    stream = torch.cuda.current_stream().cuda_stream
+    bad = ids.clone()
+    bad[1, 0] = es.n_expert + 3
+    out = torch.zeros((x.shape[0], es.n_embd), device="cuda")
+    d = op.describe(x, bad, w, out)
+    assert _lib.lib().latent_expert_ffn_forward_noalloc(C.byref(d), stream) == 0
+    assert _lib.lib().latent_expert_ffn_check_noalloc(C.byref(d), stream) == 5   # LATENT_ERR_EXPERT_ID
+    d = op.describe(x, ids, w, out)
+    assert _lib.lib().latent_expert_ffn_forward_noalloc(C.byref(d), stream) == 0
+    assert _lib.lib().latent_expert_ffn_check_noalloc(C.byref(d), stream) == 0
+
+
 def test_noalloc_rejects_batches_beyond_its_scratch(cuda):
     z = golden("moe")
     facs, _ = golden_moe_experts(z)
