@@ -2,6 +2,7 @@
 """Benchmark of the fused latent expert FFN (BASELINE metric: routed tokens/s).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+    python bench.py --only decode|prefill|router|sweep   # one leg alone (profiling runs)
 
 A step is one pass of the hot path -- routing, then the fused kernel that runs
 the four-phase latent SwiGLU chain over every routed (token, expert) pair and
@@ -17,9 +18,14 @@ so that no dirty flush lines are written back inside the timed region).  ``e2e``
 op with pinned host buffers: H2D of x/ids/weights and D2H of the output are
 inside the timed region.  ``roofline``: the dominant kernel's algorithmic
 bytes / its mean duration (CUDA events recorded between the library's kernel
-launches), against MEASURED_PEAKS.json.  ``cpu_baseline`` / ``--impl
-reference``: the reference CPU runtime's algorithm (the numpy oracle port)
-on the host cores.
+launches), against MEASURED_PEAKS.json; ``traffic`` is null (DRAM bytes are
+not measured inside this run; profiles/ holds the ncu figures).
+``cpu_baseline`` / ``--impl reference``: the reference CPU runtime's
+algorithm (the numpy oracle port) on the host cores.  Both arms print the
+same ``config`` dict; how the job is spread over GPUs is the top-level
+``parallel`` key.  Extra legs of the default 1-GPU run: ``prefill`` (config
+2, tensor-core path), ``router`` (config 3 routing shape) and ``sweep``
+(config 4 decode shapes: ranks 64/256/512, batches 1..256).
 """
 
 from __future__ import annotations
@@ -61,6 +67,10 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bound on the CPU baseline's timed work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill leg of the default run")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the config-4 decode sweep of the default run")
+    ap.add_argument("--only", choices=["decode", "prefill", "router", "sweep"],
+                    help="run one leg alone on cuda:0 and print its JSON (no CPU baseline, no e2e); "
+                         "for profiling one kernel at a time")
     ap.add_argument("--ep-exact", action="store_true",
                     help="expert parallel: exact splits with a host read of the counts (default: fixed capacity)")
     ap.add_argument("--ep-eager", action="store_true",
@@ -171,7 +181,7 @@ def allreduce_sum(v: float, world: int) -> float:
     return float(t.item())
 
 
-PHASES = ["route (k_route_single)", "fused expert chain (k_decode)"]
+PHASES = ["route (k_route_single)", "fused expert chain (k_chain)"]
 KINDS = ("gate_a", "up_a", "gate_b", "up_b", "down_a", "down_b")
 
 
@@ -201,13 +211,15 @@ def kind_bytes(es, kinds, experts):
     return sum(es[k].nbytes(experts) + es[k].int8_bytes(experts) for k in kinds)
 
 
-def config_json(cfg, ids, world, parallel):
+def config_json(cfg, ids):
+    """The workload, identical in both arms (how it is spread over GPUs is reported beside it)."""
     routed = int((ids >= 0).sum())
     return {"workload": cfg.name, "n_expert": cfg.n_expert, "n_embd": cfg.n_embd, "n_ff": cfg.n_ff,
             "rank": cfg.rank, "top_k": cfg.top_k, "tokens_per_gpu": int(ids.shape[0]),
             "routed_per_gpu": routed, "x_dtype": str(cfg.x_dtype).replace("torch.", ""),
-            "quant": "NF4 g32 + per-group INT8 below 20 dB", "l2": "flushed before every step (256 MiB write, then 256 MiB read of another buffer)",
-            "parallelism": parallel, "seed": cfg.seed}
+            "quant": "NF4 g32 + per-group INT8 below 20 dB",
+            "l2": "flushed before every step (256 MiB write, then 256 MiB read of another buffer)",
+            "seed": cfg.seed}
 
 
 def cpu_leg(cfg, es, x, ids, w, seconds: float, min_steps: int = 3):
@@ -241,17 +253,6 @@ def cpu_leg(cfg, es, x, ids, w, seconds: float, min_steps: int = 3):
             "sample": f"{len(times)} full batches of {ids.shape[0]} tokens ({routed} routed pairs), "
                       f"{len(touched)} experts pre-dequantized in {dequant_s:.2f} s",
             "ms_per_step": step * 1e3, "dequant_s": dequant_s}
-
-
-def profiled_traffic(workload):
-    """DRAM bytes per k_decode launch from the committed ncu summary of this workload, else None."""
-    f = ROOT / "profiles" / "k_decode_c1.md"
-    if workload != "c1-v2lite-decode" or not f.exists():
-        return None
-    for line in f.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            return int(line.split(":")[1])
-    return None
 
 
 def run_ours(args, world, rank, local):
@@ -329,9 +330,9 @@ def run_ours(args, world, rank, local):
         "metric": METRIC, "value": routed_all / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE recipe)",
-        "config": config_json(cfg, ids, world, "replicas" if world > 1 else "single GPU"),
+        "config": config_json(cfg, ids), "parallel": "single GPU",
         "roofline": {"bound": "hbm", "kernel": PHASES[dom], "achieved": ach, "peak": pk["hbm_gbs"],
-                     "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "traffic": profiled_traffic(cfg.name),
+                     "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "traffic": None,
                      "algorithmic_bytes": op_bytes, "mean_ms": float(phase_ms[dom]),
                      "peak_source": pk["source"]},
         "roofline_op": {"achieved": op_ach, "frac": op_ach / pk["hbm_gbs"], "unit": "GB/s",
@@ -349,11 +350,54 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_leg(cfg, es, x, ids, w, args.cpu_seconds)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
-    if world == 1 and args.config == 1 and not args.no_prefill:
+    if world == 1 and args.config == 1 and not (args.no_prefill and args.no_sweep):
         del es, op
         torch.cuda.empty_cache()
-        line["prefill"] = run_prefill(args, 2, dev, steps=max(5, min(args.steps, 20)), warmup=args.warmup)
+        if not args.no_prefill:
+            line["prefill"] = run_prefill(args, 2, dev, steps=max(5, min(args.steps, 20)), warmup=args.warmup)
+            torch.cuda.empty_cache()
+        if not args.no_sweep:
+            line["sweep"] = run_sweep(dev, flush, steps=max(5, min(args.steps, 20)), warmup=max(args.warmup, 3))
     return line
+
+
+SWEEP_POINTS = ((256, (1, 8, 64, 256)), (64, (64,)), (512, (64,)))
+
+
+def run_sweep(dev, flush, steps: int, warmup: int):
+    """Decode path on config 4's layer (256 experts, d 7168, f 2048, top-8) at several ranks and batch
+    sizes: routed tokens/s and the whole op's algorithmic bytes (touched experts' factors + x + out)
+    over its event time, against the HBM peak."""
+    from latent_b200 import ExpertFFN, synth
+    pk = peaks()
+    out = []
+    for rank, batches in SWEEP_POINTS:
+        es = synth.make_expert_set(synth.sweep_config(rank, 1), device=dev)
+        op = ExpertFFN(es, path="decode")
+        for b in batches:
+            cfg = synth.sweep_config(rank, b)
+            x, ids, w = synth.make_batch(cfg, dev)
+            for _ in range(warmup):
+                op(x, ids, w)
+            op.check()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+            for a, e in ev:
+                flush()
+                a.record()
+                op(x, ids, w)
+                e.record()
+            torch.cuda.synchronize()
+            ms = statistics.mean(a.elapsed_time(e) for a, e in ev)
+            touched = sorted(set(ids[ids >= 0].cpu().tolist()))
+            nbytes = kind_bytes(es, KINDS, touched) + x.numel() * x.element_size() + x.shape[0] * cfg.n_embd * 4
+            routed = int((ids >= 0).sum())
+            out.append({"workload": cfg.name, "rank": rank, "tokens": b, "routed": routed,
+                        "experts_touched": len(touched), "ms": ms, "value": routed / (ms * 1e-3), "unit": UNIT,
+                        "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / (ms * 1e-3) / 1e9,
+                        "frac_hbm": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"]})
+        del es, op
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_router(dev, flush, steps: int, warmup: int, T: int = 16384, E: int = 256, k: int = 8):
@@ -561,9 +605,10 @@ def run_ours_ep(args, world, rank, local):
         "metric": METRIC, "value": routed_all / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE recipe)",
-        "config": config_json(cfg, ids, world, f"expert-parallel ep{world} (NCCL all-to-all, "
-                              f"{'exact splits' if args.ep_exact else 'fixed capacity'}"
-                              f"{', CUDA graph' if not args.ep_eager and not args.ep_exact else ''})"),
+        "config": config_json(cfg, ids),
+        "parallel": (f"expert-parallel ep{world} (NCCL all-to-all, "
+                     f"{'exact splits' if args.ep_exact else 'fixed capacity'}"
+                     f"{', CUDA graph' if not args.ep_eager and not args.ep_exact else ''})"),
         "roofline": {"bound": "hbm", "kernel": "local fused expert FFN (rank 0)", "achieved": ach,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "traffic": None,
                      "algorithmic_bytes": local_bytes, "mean_ms": ffn_ms, "peak_source": pk["source"]},
@@ -588,14 +633,45 @@ def run_reference(args, world, rank, local):
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE recipe)",
-        "config": config_json(cfg, ids, world, "host CPU"),
+        "config": config_json(cfg, ids), "parallel": f"host CPU ({cb['cores']} threads)",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cb["cores"], "kind": "port", "sample": cb["sample"]},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
+def run_only(args):
+    """One leg alone on cuda:0 (profiling): the op runs warm-up + steps times, nothing else is timed."""
+    dev = torch.device("cuda", 0)
+    flush = L2Flush(dev)
+    steps, warmup = args.steps, args.warmup
+    if args.only == "router":
+        return {"router": run_router(dev, flush, steps=steps, warmup=warmup)}
+    if args.only == "prefill":
+        return {"prefill": run_prefill(args, 2, dev, steps=steps, warmup=warmup)}
+    if args.only == "sweep":
+        return {"sweep": run_sweep(dev, flush, steps=steps, warmup=warmup)}
+    from latent_b200 import ExpertFFN
+    cfg, es, x, ids, w, _ = workload(args.config, dev, 0)
+    op = ExpertFFN(es, path="decode")
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for k in range(warmup + steps):
+        flush()
+        if k >= warmup:
+            ev[k - warmup][0].record()
+        op(x, ids, w)
+        if k >= warmup:
+            ev[k - warmup][1].record()
+    op.check()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    return {"decode": {"workload": cfg.name, "ms": ms, "value": int((ids >= 0).sum()) / (ms * 1e-3), "unit": UNIT}}
+
+
 def main() -> int:
     args = parse_args()
+    if args.only:
+        torch.cuda.set_device(0)
+        print(json.dumps(run_only(args)), flush=True)
+        return 0
     world, rank, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":

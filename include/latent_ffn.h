@@ -199,6 +199,60 @@ LATENT_API int latent_ep_pack_fixed(const latent_ep_desc *desc, int32_t world, i
 LATENT_API int latent_ep_combine_fixed(const latent_ep_desc *desc, int32_t world, int32_t cap, const float *y_rows,
                                        float *out, struct CUstream_st *stream);
 
+/* Dense-fallback experts (reference: the compressor keeps a dense fp16
+ * copy `<name>.dense_fallback` of a matrix whose factors miss its error
+ * threshold, loader/latent_loader.py:262-265; the dense forward is
+ * dense_swiglu_expert, loader/latent_runtime.py:62-73; the reference runtime
+ * itself ignores the copy).  A flagged expert is served densely: per kind,
+ * its dense matrix when present, else its factor pair as exact fp32 A and B
+ * (dequantised once at load).  Use with the latent op on the same batch:
+ *   1. latent_dense_experts_prepare: routes the flagged experts' slots into
+ *      the workspace and writes ids_latent = ids with those slots set to -1;
+ *   2. latent_expert_ffn_forward with ids_latent (writes out);
+ *   3. latent_dense_experts_forward: adds the flagged experts' contributions
+ *      into out (OUT_PER_SLOT: writes their rows), fp32 accumulation on the
+ *      CUDA cores.  Same desc and workspace as step 1. */
+typedef struct latent_dense_expert {
+    int32_t expert;          /* global expert id */
+    int32_t rank;            /* rank of the pairs below (even; unused when all kinds are dense) */
+    const void *dense[3];    /* gate [d][f], up [d][f], down [f][d] (dense_type); NULL: the pair */
+    const float *a[3];       /* A of the kinds without a dense matrix: [d][r], [d][r], [f][r] fp32 */
+    const float *b[3];       /* B: [r][f], [r][f], [r][d] fp32 */
+} latent_dense_expert;
+
+typedef struct latent_dense_desc {
+    int32_t n_expert;        /* E */
+    int32_t n_embd;          /* d (multiple of 32) */
+    int32_t n_ff;            /* f (multiple of 32) */
+    int32_t n_tokens;        /* T */
+    int32_t top_k;           /* k */
+    int32_t x_type;          /* latent_type of x */
+    int32_t w_type;          /* latent_type of the router weights (F32 or F16) */
+    int32_t dense_type;      /* LATENT_TYPE_F16 or F32: element type of the dense matrices */
+    uint32_t flags;          /* LATENT_FLAG_WEIGHT_BEFORE_DOWN, LATENT_FLAG_OUT_PER_SLOT */
+    int32_t n_dense;         /* flagged experts */
+    const latent_dense_expert *experts;  /* host array [n_dense] */
+    const int32_t *dense_index;          /* device [E]: index into experts, -1 for latent experts */
+    const void *x;           /* [T][d] */
+    const int32_t *ids;      /* [T][k] (the caller's ids, not ids_latent) */
+    const void *weights;     /* [T][k] */
+    float *out;              /* as for latent_expert_ffn_forward */
+    void *workspace;         /* 256-byte aligned, latent_dense_workspace_size() bytes */
+    size_t workspace_bytes;
+} latent_dense_desc;
+
+LATENT_API int latent_dense_workspace_size(const latent_dense_desc *desc, size_t *bytes);
+LATENT_API int latent_dense_experts_prepare(const latent_dense_desc *desc, int32_t *ids_latent,
+                                            struct CUstream_st *stream);
+LATENT_API int latent_dense_experts_forward(const latent_dense_desc *desc, struct CUstream_st *stream);
+
+/* y[M][N] = x[M][K] . w[K][N] in fp32 on the CUDA cores (x F32/F16/BF16,
+ * w F32/F16, row-major, K and N even).  The projection utility behind the
+ * Python mirror's project (loader/latent_runtime.py:35-36, on dequantised
+ * factors) and dense_swiglu_expert (:62-73). */
+LATENT_API int latent_dense_matmul(const void *x, int32_t x_type, const void *w, int32_t w_type, float *y, int64_t M,
+                                   int64_t K, int64_t N, struct CUstream_st *stream);
+
 /* ABI version of the loaded library (LATENT_ABI_VERSION). */
 LATENT_API int latent_abi_version(void);
 
@@ -294,7 +348,10 @@ LATENT_API int latent_pack_tiles(const uint8_t *codes, const uint16_t *scales, i
  * top_k < 1 or top_k > n_expert (the reference raises ValueError),
  * LATENT_ERR_INVALID for threshold outside (0, 1] (ValueError there) or
  * unknown flags, LATENT_ERR_UNSUPPORTED beyond 1024 experts or top_k 32.
- * Scores are expected finite; a NaN score is never selected.  Stream-ordered,
+ * NaN scores rank below every number (numpy's sort order), so they are
+ * selected only when fewer than top_k numbers remain; a token whose top_k
+ * then holds a NaN keeps all top_k slots with NaN weights, as the reference
+ * does.  Stream-ordered,
  * allocates nothing; ids/weights feed latent_expert_ffn_forward directly. */
 enum { LATENT_ROUTER_RENORMALIZE = 1u << 0 };
 LATENT_API int latent_router_topk(const float *scores, int32_t n_tokens, int32_t n_expert, int32_t top_k,

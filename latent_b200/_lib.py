@@ -70,6 +70,39 @@ class FfnDesc(C.Structure):
     ]
 
 
+class DenseExpert(C.Structure):
+    _fields_ = [
+        ("expert", C.c_int32),
+        ("rank", C.c_int32),
+        ("dense", C.c_void_p * 3),
+        ("a", C.c_void_p * 3),
+        ("b", C.c_void_p * 3),
+    ]
+
+
+class DenseDesc(C.Structure):
+    _fields_ = [
+        ("n_expert", C.c_int32),
+        ("n_embd", C.c_int32),
+        ("n_ff", C.c_int32),
+        ("n_tokens", C.c_int32),
+        ("top_k", C.c_int32),
+        ("x_type", C.c_int32),
+        ("w_type", C.c_int32),
+        ("dense_type", C.c_int32),
+        ("flags", C.c_uint32),
+        ("n_dense", C.c_int32),
+        ("experts", C.POINTER(DenseExpert)),
+        ("dense_index", C.c_void_p),
+        ("x", C.c_void_p),
+        ("ids", C.c_void_p),
+        ("weights", C.c_void_p),
+        ("out", C.c_void_p),
+        ("workspace", C.c_void_p),
+        ("workspace_bytes", C.c_size_t),
+    ]
+
+
 class EpDesc(C.Structure):
     _fields_ = [
         ("n_expert", C.c_int32),
@@ -98,6 +131,11 @@ EXPORTS.update({
     "latent_ep_dispatch": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_ep_combine": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_ep_check": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
+    "latent_dense_workspace_size": (C.c_int, [C.POINTER(DenseDesc), C.POINTER(C.c_size_t)]),
+    "latent_dense_experts_prepare": (C.c_int, [C.POINTER(DenseDesc), C.c_void_p, C.c_void_p]),
+    "latent_dense_experts_forward": (C.c_int, [C.POINTER(DenseDesc), C.c_void_p]),
+    "latent_dense_matmul": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_void_p, C.c_int64,
+                                      C.c_int64, C.c_int64, C.c_void_p]),
     "latent_abi_version": (C.c_int, []),
     "latent_status_string": (C.c_char_p, [C.c_int]),
     "latent_expert_ffn_workspace_size": (C.c_int, [C.POINTER(FfnDesc), C.POINTER(C.c_size_t)]),

@@ -10,7 +10,8 @@
 // k rounds of a warp arg-max (two warp reductions: the largest order-
 // preserving key, then the lowest expert id holding it; only the winning
 // lane rescans) produce the descending top-k, which lane 0 then scans with
-// the reference's arithmetic: the total is numpy's
+// the reference's arithmetic (a NaN among the top k makes the total NaN, and
+// every slot is kept, as in the reference): the total is numpy's
 // float32 pairwise sum, the target threshold x total is formed in double and
 // compared in float32, the running sum is float32.  Lane i writes slot i.
 // Traffic: one read of the scores, k ids + k weights written per token.
@@ -50,7 +51,9 @@ __device__ float f32_sum(const float *a, int n) {
 
 // Order-preserving 32-bit key of a finite or infinite score: a larger score
 // has a larger key, -0 and +0 share one key, and no score maps to 0 (the
-// mark for "nothing left to select").
+// mark for "nothing left to select") or 1 (the key of NaN, below -inf: numpy's
+// sort places NaN after every number, so the reference picks NaN scores only
+// when fewer than k others remain, lowest expert id first).
 __device__ __forceinline__ unsigned score_key(float v) {
     const unsigned b = v == 0.f ? 0u : __float_as_uint(v);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
@@ -69,12 +72,12 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(const float *
     if (t >= T) return;
     const float *row = scores + (size_t)t * E;
     float v[NPL];
-    unsigned key[NPL];    // 0: padding, NaN or already selected
+    unsigned key[NPL];    // 0: padding or already selected; 1: NaN
 #pragma unroll
     for (int j = 0; j < NPL; ++j) {
         const int e = j * 32 + lane;
         v[j] = e < E ? __ldg(row + e) : 0.f;
-        key[j] = (e >= E || v[j] != v[j]) ? 0u : score_key(v[j]);
+        key[j] = e >= E ? 0u : v[j] != v[j] ? 1u : score_key(v[j]);
     }
     // each lane's best remaining element (lowest index among equal scores)
     unsigned lkey = 0;
@@ -101,9 +104,9 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(const float *
         const unsigned m = __reduce_max_sync(full, lkey);
         const unsigned win = __reduce_min_sync(full, lkey == m ? (unsigned)(lj * 32 + lane) : 0xffffffffu);
         const bool none = m == 0u;
-        // the score back from its key; a zero score takes the winner's own bits (keeps the sign of -0)
+        // the score back from its key; a zero or NaN score takes the winner's own bits (the sign of -0, the payload)
         float val = __uint_as_float((m & 0x80000000u) ? (m & 0x7fffffffu) : ~m);
-        if (m == 0x80000000u) val = __shfl_sync(full, value_at(lj), (int)(win & 31u));
+        if (m == 0x80000000u || m == 1u) val = __shfl_sync(full, value_at(lj), (int)(win & 31u));
         if (!none && lane == (int)(win & 31u)) {
 #pragma unroll
             for (int j = 0; j < NPL; ++j) key[j] = j == lj ? 0u : key[j];

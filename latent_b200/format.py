@@ -35,7 +35,7 @@ becomes two 32-element groups carrying the same fp16 scale.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import List, Mapping, Optional, Sequence
+from typing import Dict, List, Mapping, Optional, Sequence
 
 import numpy as np
 import torch
@@ -292,9 +292,17 @@ class ExpertSet:
     ``rank`` is the padded rank every expert is stored at (a power of two
     between 32 and 512); experts of lower rank carry zero groups, which do
     not change any result.
+
+    ``dense`` flags dense-fallback experts: ``{expert: {"gate": W_g [d, f],
+    "up": W_u [d, f], "down": W_d [f, d]}}`` with any subset of the three
+    kinds (the reference's ``<name>.dense_fallback`` copies,
+    loader/latent_loader.py:262-265, kept as fp16 on the device).  The routed
+    op serves a flagged expert densely: its dense matrices where given, its
+    exact factor pairs for the other kinds.
     """
 
-    def __init__(self, experts: Sequence[Mapping[str, GroupedFactor]], device="cuda", rank: Optional[int] = None):
+    def __init__(self, experts: Sequence[Mapping[str, GroupedFactor]], device="cuda", rank: Optional[int] = None,
+                 dense: Optional[Mapping[int, Mapping[str, object]]] = None):
         if not experts:
             raise ValueError("an ExpertSet needs at least one expert")
         d, r0 = experts[0]["gate_a"].rows, experts[0]["gate_a"].cols
@@ -322,6 +330,23 @@ class ExpertSet:
             dev = torch.device("cuda", torch.cuda.current_device())
         self.device = dev
         self.factors = {k: StackedFactor([ex[k].padded(*shapes[k]) for ex in experts], self.device) for k in KINDS}
+        dense_shapes = {"gate": (d, f), "up": (d, f), "down": (f, d)}
+        self.dense: Dict[int, Dict[str, torch.Tensor]] = {}
+        for e, mats in (dense or {}).items():
+            e = int(e)
+            if not 0 <= e < self.n_expert:
+                raise ValueError(f"dense-fallback expert {e} out of range [0, {self.n_expert})")
+            kept = {}
+            for name, w in mats.items():
+                if name not in dense_shapes:
+                    raise ValueError(f"unknown dense kind {name!r} (gate, up or down)")
+                w = torch.as_tensor(np.asarray(w) if not torch.is_tensor(w) else w)
+                if tuple(w.shape) != dense_shapes[name]:
+                    raise ValueError(f"dense {name} of expert {e} has shape {tuple(w.shape)}, "
+                                     f"expected {dense_shapes[name]}")
+                kept[name] = w.to(device=self.device, dtype=torch.float16).contiguous()
+            if kept:
+                self.dense[e] = kept
 
     def __getitem__(self, kind: str) -> StackedFactor:
         return self.factors[kind]

@@ -43,21 +43,62 @@ def _stream_ptr(device: torch.device) -> int:
 
 @dataclass
 class FactorPair:
-    """A low-rank pair W ~= A @ B kept packed on the device (reference FactorPair, latent_runtime.py:13-16)."""
+    """A low-rank pair W ~= A @ B kept packed on the device (reference FactorPair, latent_runtime.py:13-16).
+
+    ``dense``: the matrix's dense-fallback copy (fp16 on the device) when it
+    was loaded with ``load_pair(..., dense_fallback=True)``; ``project`` then
+    uses it instead of the factors.
+    """
 
     a: GroupedFactor
     b: GroupedFactor
     _sets: Dict[Tuple[int, int], ExpertSet] = field(default_factory=dict, repr=False, compare=False)
+    dense: Optional[torch.Tensor] = None
 
 
-def load_pair(arrays: Mapping[str, np.ndarray], name: str, device=None) -> FactorPair:
+def load_pair(arrays: Mapping[str, np.ndarray], name: str, device=None, dense_fallback: bool = False) -> FactorPair:
     """Reference-NPZ factors ``<name>.{a,b}.*`` -> device pair (latent_runtime.py:19-32).
 
     NF4 (group 32) is used when present, else INT8 (group 64); a missing
-    factor raises ``KeyError`` like the reference.
+    factor raises ``KeyError`` like the reference.  With ``dense_fallback``
+    the pair also carries ``<name>.dense_fallback`` when the artifact has one
+    (loader/latent_loader.py:262-265; the reference runtime ignores it, as
+    this function does by default).
     """
     dev = _device(device)
-    return FactorPair(from_npz(arrays, name, "a").to(dev), from_npz(arrays, name, "b").to(dev))
+    pair = FactorPair(from_npz(arrays, name, "a").to(dev), from_npz(arrays, name, "b").to(dev))
+    key = f"{name}.dense_fallback"
+    if dense_fallback and key in arrays:
+        pair.dense = torch.as_tensor(np.asarray(arrays[key])).to(device=dev, dtype=torch.float16).contiguous()
+    return pair
+
+
+def _matmul(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x [M, K] (f32/f16/bf16) @ w [K, N] (f32/f16) -> fp32 [M, N] by latent_dense_matmul."""
+    if w.dtype not in _W_TYPES:
+        w = w.float()
+    if x.dtype not in _X_TYPES:
+        x = x.float()
+    M, K = x.shape
+    if w.shape[0] != K:
+        raise ValueError(f"matmul shapes {tuple(x.shape)} @ {tuple(w.shape)} do not match")
+    N = w.shape[1]
+    if K % 2:  # the kernel reads column pairs: a zero row/column pair changes no sum
+        x = torch.nn.functional.pad(x, (0, 1))
+        w = torch.nn.functional.pad(w, (0, 0, 0, 1))
+    if N % 2:
+        w = torch.nn.functional.pad(w, (0, 1))
+    x, w = x.contiguous(), w.contiguous()
+    Kp, Np = w.shape
+    y = torch.empty((M, Np), dtype=torch.float32, device=w.device)
+    _lib.check(_lib.lib().latent_dense_matmul(x.data_ptr(), _X_TYPES[x.dtype], w.data_ptr(), _W_TYPES[w.dtype],
+                                              y.data_ptr(), M, Kp, Np, _stream_ptr(w.device)), "latent_dense_matmul")
+    return y[:, :N] if Np != N else y
+
+
+def _rows(x: torch.Tensor, k: int) -> Tuple[torch.Tensor, tuple]:
+    lead = tuple(x.shape[:-1])
+    return x.reshape(-1, k), lead
 
 
 def dequantize(factor, expert: int = 0) -> torch.Tensor:
@@ -114,17 +155,18 @@ def project(x, pair: FactorPair):
     """(x @ A) @ B in fp32 (latent_runtime.py:35-36).
 
     A utility: A and B are dequantized bit-exactly by the CUDA library and
-    multiplied with fp32 GEMMs (TF32 off).  The fused expert path never
-    materialises the factors.
+    multiplied by its fp32 CUDA-core GEMM (latent_dense_matmul); a pair
+    loaded with its dense-fallback copy multiplies by that instead.  The
+    fused expert path never materialises the factors.
     """
     dev = pair.a.lo.device
     xt, host = _as_device_f32(x, dev)
-    prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = False
-    try:
-        y = (xt @ dequantize(pair.a)) @ dequantize(pair.b)
-    finally:
-        torch.backends.cuda.matmul.allow_tf32 = prev
+    x2, lead = _rows(xt, xt.shape[-1])
+    if pair.dense is not None:
+        y = _matmul(x2, pair.dense)
+    else:
+        y = _matmul(_matmul(x2, dequantize(pair.a)), dequantize(pair.b))
+    y = y.reshape(*lead, y.shape[-1])
     return y.cpu().numpy() if host else y
 
 
@@ -132,16 +174,13 @@ def dense_swiglu_expert(x, gate, up, down, weight: float = 1.0, weight_before_do
     """Dense SwiGLU reference on the device (latent_runtime.py:62-73); the dense-fallback expert form."""
     dev = _device(gate.device if torch.is_tensor(gate) and gate.is_cuda else None)
     xt, host = _as_device_f32(x, dev)
-    g, u, dn = (_as_device_f32(m, dev)[0] for m in (gate, up, down))
-    prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = False
-    try:
-        h = silu(xt @ g) * (xt @ u)
-        if weight_before_down:
-            h = h * torch.as_tensor(weight, dtype=torch.float32, device=dev)
-        y = h @ dn
-    finally:
-        torch.backends.cuda.matmul.allow_tf32 = prev
+    g, u, dn = (m.to(dev) if torch.is_tensor(m) and m.dtype in _W_TYPES else _as_device_f32(m, dev)[0]
+                for m in (gate, up, down))
+    x2, lead = _rows(xt, xt.shape[-1])
+    h = silu(_matmul(x2, g)) * _matmul(x2, u)
+    if weight_before_down:
+        h = h * torch.as_tensor(weight, dtype=torch.float32, device=dev)
+    y = _matmul(h, dn).reshape(*lead, dn.shape[-1])
     return y.cpu().numpy() if host else y
 
 
@@ -183,6 +222,9 @@ class ExpertFFN:
         self.path = _PATHS[path]
         self._ws: Optional[torch.Tensor] = None
         self._last_desc: Optional[_lib.FfnDesc] = None
+        self._dense = None      # dense-fallback tables (built on first use)
+        self._dws: Optional[torch.Tensor] = None
+        self._keep = None
 
     def _workspace(self, nbytes: int) -> torch.Tensor:
         if self._ws is None or self._ws.numel() < nbytes:
@@ -224,15 +266,69 @@ class ExpertFFN:
             out = torch.empty(shape, dtype=torch.float32, device=self.experts.device)
         elif tuple(out.shape) != shape or out.dtype != torch.float32:
             raise ValueError(f"out must be float32 {shape}")
+        if self.experts.dense:
+            return self._call_mixed(x, ids, weights, weight_before_down, out_per_slot, out)
         d = self.describe(x, ids, weights, out, weight_before_down, out_per_slot)
         self._last_desc = d
         _lib.check(_lib.lib().latent_expert_ffn_forward(C.byref(d), _stream_ptr(self.experts.device)),
                    "latent_expert_ffn_forward")
         return out
 
+    def _dense_tables(self):
+        """latent_dense_expert entries of the set's dense-fallback experts (built once)."""
+        if self._dense is None:
+            es = self.experts
+            flagged = sorted(es.dense)
+            arr = (_lib.DenseExpert * len(flagged))()
+            keep = []
+            index = torch.full((es.n_expert,), -1, dtype=torch.int32)
+            for i, e in enumerate(flagged):
+                index[e] = i
+                arr[i].expert, arr[i].rank = e, es.rank
+                for m, name in enumerate(("gate", "up", "down")):
+                    w = es.dense[e].get(name)
+                    if w is not None:
+                        arr[i].dense[m] = w.data_ptr()
+                    else:  # the kind keeps its factors: exact fp32 A and B
+                        a, b = dequantize(es[f"{name}_a"], e), dequantize(es[f"{name}_b"], e)
+                        keep += [a, b]
+                        arr[i].a[m], arr[i].b[m] = a.data_ptr(), b.data_ptr()
+            self._dense = (arr, index.to(es.device), keep)
+        return self._dense
+
+    def _call_mixed(self, x, ids, weights, wbd, per_slot, out):
+        """Latent experts through the fused op, dense-fallback experts through the dense kernels."""
+        arr, index, _ = self._dense_tables()
+        es = self.experts
+        T, k = ids.shape
+        dd = _lib.DenseDesc()
+        dd.n_expert, dd.n_embd, dd.n_ff, dd.n_tokens, dd.top_k = es.n_expert, es.n_embd, es.n_ff, T, k
+        dd.x_type, dd.w_type, dd.dense_type = _X_TYPES[x.dtype], _W_TYPES[weights.dtype], _lib.TYPE_F16
+        dd.flags = (_lib.FLAG_WEIGHT_BEFORE_DOWN if wbd else 0) | (_lib.FLAG_OUT_PER_SLOT if per_slot else 0)
+        dd.n_dense, dd.experts, dd.dense_index = len(arr), arr, index.data_ptr()
+        dd.x, dd.ids, dd.weights, dd.out = x.data_ptr(), ids.data_ptr(), weights.data_ptr(), out.data_ptr()
+        n = C.c_size_t(0)
+        _lib.check(_lib.lib().latent_dense_workspace_size(C.byref(dd), C.byref(n)), "latent_dense_workspace_size")
+        if self._dws is None or self._dws.numel() < n.value:
+            self._dws = torch.empty(max(int(n.value), 256), dtype=torch.uint8, device=es.device)
+        dd.workspace, dd.workspace_bytes = self._dws.data_ptr(), self._dws.numel()
+        stream = _stream_ptr(es.device)
+        ids_latent = torch.empty_like(ids)
+        _lib.check(_lib.lib().latent_dense_experts_prepare(C.byref(dd), ids_latent.data_ptr(), stream),
+                   "latent_dense_experts_prepare")
+        d = self.describe(x, ids_latent, weights, out, wbd, per_slot)
+        self._last_desc = d
+        self._keep = ids_latent
+        _lib.check(_lib.lib().latent_expert_ffn_forward(C.byref(d), stream), "latent_expert_ffn_forward")
+        _lib.check(_lib.lib().latent_dense_experts_forward(C.byref(dd), stream), "latent_dense_experts_forward")
+        return out
+
     def call_timed(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, events,
                    weight_before_down: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """Like ``__call__``; records ``events`` (recorded torch.cuda.Event objects) around every kernel."""
+        """Like ``__call__``; records ``events`` (recorded torch.cuda.Event objects) around every kernel
+        (layers without dense-fallback experts)."""
+        if self.experts.dense:
+            raise ValueError("call_timed serves layers without dense-fallback experts")
         T, k = ids.shape
         if out is None:
             out = torch.empty((T, self.experts.n_embd), dtype=torch.float32, device=self.experts.device)

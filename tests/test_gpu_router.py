@@ -63,6 +63,30 @@ def test_router_ties_zero_rows_and_empty(cuda):
     assert ids.shape == (0, 2) and nk.shape == (0,)
 
 
+def test_router_nan_rows_follow_numpy_sort_order(cuda):
+    """numpy's argsort places NaN after every number: a NaN is picked only
+    when fewer than k numbers remain, and then the NaN total keeps all k
+    slots with NaN weights."""
+    rng = np.random.default_rng(6)
+    scores = rng.random((6, 48)).astype(np.float32)
+    scores[1, 7] = np.nan                         # one NaN, k numbers left: never picked
+    scores[2, 3:] = np.nan                        # 3 numbers, then NaN in expert order
+    scores[3, :] = np.nan                         # all NaN
+    scores[4, ::2] = np.nan
+    for renorm in (True, False):
+        ids, w, nk = _run(scores, 6, 0.8, renorm)
+        ids_o, w_o, nk_o = O.router_topk(scores, 6, 0.8, renormalize=renorm)
+        assert np.array_equal(ids, ids_o) and np.array_equal(nk, nk_o)
+        assert np.array_equal(np.isnan(w), np.isnan(w_o))
+        fin = ~np.isnan(w_o)
+        assert np.array_equal(w[fin].view(np.uint32), w_o[fin].view(np.uint32))
+        assert sorted(ids[2][:3]) == [0, 1, 2] and list(ids[2][3:]) == [3, 4, 5] and nk[2] == 6
+        assert np.isnan(w[2]).all() == renorm
+        assert 7 not in ids[1]
+    ids, w, nk = router_topk(torch.empty((0, 16), device="cuda"), 2)
+    assert ids.shape == (0, 2) and nk.shape == (0,)
+
+
 def test_router_feeds_the_fused_op(cuda):
     """Router output straight into the fused op equals the oracle MoE on the same routing."""
     from latent_b200 import ExpertFFN, ExpertSet
