@@ -253,6 +253,39 @@ LATENT_API int latent_dense_experts_forward(const latent_dense_desc *desc, struc
 LATENT_API int latent_dense_matmul(const void *x, int32_t x_type, const void *w, int32_t w_type, float *y, int64_t M,
                                    int64_t K, int64_t N, struct CUstream_st *stream);
 
+/* ggml op adapter: the body of the reference's ggml_cuda_latent_expert_ffn
+ * (kernels/latent_fused_expert_ffn.cu:134-292) as library calls.  A ggml
+ * tensor is passed as its device data, its ne[4] and its ggml_type value. */
+typedef struct latent_ggml_tensor {
+    const void *data;
+    int64_t ne[4];
+    int32_t type;           /* LATENT_GGML_* (the ggml_type enum values) */
+} latent_ggml_tensor;
+enum { LATENT_GGML_F32 = 0, LATENT_GGML_F16 = 1, LATENT_GGML_I8 = 24, LATENT_GGML_I32 = 26, LATENT_GGML_BF16 = 30 };
+
+/* Load time.  factors[12] = the op's src[3..14] (codes I8 and scales F16 of
+ * gate_a, gate_b, up_a, up_b, down_a, down_b) as the reference GGUF writer
+ * stores them (loader/write_latent_gguf.py:101-123, :412-436): dims recorded
+ * as ne = (n_expert, rows, cols/2) and (n_expert, rows, cols/32), bytes in C
+ * order of those dims, A factors [n_in, max_rank], B factors [rank, n_out].
+ * Copies them into `dst` (caller-owned device memory, 256-byte aligned) in
+ * the library's tile order, padded to one power-of-two rank with zero groups,
+ * and fills the layer fields of *desc (n_expert, n_embd, n_ff, rank and the
+ * six latent_qmatrix).  dst == NULL: only *bytes_needed is written.
+ * Stream-ordered; the sources may be freed once the stream has passed it. */
+LATENT_API int latent_ggml_pack_layer(const latent_ggml_tensor *factors, void *dst, size_t dst_bytes,
+                                      size_t *bytes_needed, latent_ffn_desc *desc, struct CUstream_st *stream);
+
+/* Per call.  src[3] = the op's x [n_embd, T] (F16, BF16 or F32), ids [k, T]
+ * I32, weights [k, T] (F16 or F32); dst F32 [n_embd, k, T] (the op's
+ * per-slot output, LATENT_FLAG_OUT_PER_SLOT) or [n_embd, T] (combined by
+ * the library).  `layer` comes from latent_ggml_pack_layer.  workspace ==
+ * NULL: only *workspace_needed is written; else runs
+ * latent_expert_ffn_forward on `stream`. */
+LATENT_API int latent_ggml_expert_ffn(const latent_ffn_desc *layer, const latent_ggml_tensor *src,
+                                      const latent_ggml_tensor *dst, void *workspace, size_t workspace_bytes,
+                                      size_t *workspace_needed, struct CUstream_st *stream);
+
 /* ABI version of the loaded library (LATENT_ABI_VERSION). */
 LATENT_API int latent_abi_version(void);
 

@@ -103,6 +103,17 @@ class DenseDesc(C.Structure):
     ]
 
 
+class GgmlTensor(C.Structure):
+    _fields_ = [
+        ("data", C.c_void_p),
+        ("ne", C.c_int64 * 4),
+        ("type", C.c_int32),
+    ]
+
+
+GGML_F32, GGML_F16, GGML_I8, GGML_I32, GGML_BF16 = 0, 1, 24, 26, 30
+
+
 class EpDesc(C.Structure):
     _fields_ = [
         ("n_expert", C.c_int32),
@@ -132,6 +143,10 @@ EXPORTS.update({
     "latent_ep_combine": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_ep_check": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_dense_workspace_size": (C.c_int, [C.POINTER(DenseDesc), C.POINTER(C.c_size_t)]),
+    "latent_ggml_pack_layer": (C.c_int, [C.POINTER(GgmlTensor), C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t),
+                                         C.POINTER(FfnDesc), C.c_void_p]),
+    "latent_ggml_expert_ffn": (C.c_int, [C.POINTER(FfnDesc), C.POINTER(GgmlTensor), C.POINTER(GgmlTensor),
+                                         C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t), C.c_void_p]),
     "latent_dense_experts_prepare": (C.c_int, [C.POINTER(DenseDesc), C.c_void_p, C.c_void_p]),
     "latent_dense_experts_forward": (C.c_int, [C.POINTER(DenseDesc), C.c_void_p]),
     "latent_dense_matmul": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_void_p, C.c_int64,
