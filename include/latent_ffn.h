@@ -286,6 +286,22 @@ LATENT_API int latent_ggml_expert_ffn(const latent_ffn_desc *layer, const latent
                                       const latent_ggml_tensor *dst, void *workspace, size_t workspace_bytes,
                                       size_t *workspace_needed, struct CUstream_st *stream);
 
+/* Load-time quantisation of float factors (reference encoders,
+ * loader/latent_loader.py:111-158, applied per 32-element group; no
+ * counterpart kernel in the reference).  values: n_groups x 32 fp32
+ * (row-major groups of a [rows][cols] factor, cols % 32 == 0).  Per group:
+ * NF4 codes (absmax, fp32 normalise, nearest level, lowest code on ties,
+ * fp16 scale); with snr_db not NaN, a group whose NF4 amplitude SNR
+ * ||v|| / max(||v - nf4(v)||, 1e-12) (:173-185; in fp32)
+ * is below 10^(snr_db/20) is stored INT8 instead (scale absmax/127,
+ * round-half-even, clip +-127); an all-zero group stays NF4.  Writes
+ * lo[n_groups][16] (NF4 codes, or the INT8 low nibbles), hi[n_groups][16]
+ * (INT8 high nibbles, else 0), the fp16 scale bits, is_int8[n_groups] (0/1)
+ * and, when snr is not NULL, each group's NF4 SNR: the GroupedFactor arrays
+ * of the Python layer. */
+LATENT_API int latent_quantize_groups(const float *values, int64_t n_groups, float snr_db, uint8_t *lo, uint8_t *hi,
+                                      uint16_t *scales, uint8_t *is_int8, float *snr, struct CUstream_st *stream);
+
 /* ABI version of the loaded library (LATENT_ABI_VERSION). */
 LATENT_API int latent_abi_version(void);
 

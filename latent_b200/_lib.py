@@ -143,6 +143,8 @@ EXPORTS.update({
     "latent_ep_combine": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_ep_check": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_dense_workspace_size": (C.c_int, [C.POINTER(DenseDesc), C.POINTER(C.c_size_t)]),
+    "latent_quantize_groups": (C.c_int, [C.c_void_p, C.c_int64, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_void_p, C.c_void_p]),
     "latent_ggml_pack_layer": (C.c_int, [C.POINTER(GgmlTensor), C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t),
                                          C.POINTER(FfnDesc), C.c_void_p]),
     "latent_ggml_expert_ffn": (C.c_int, [C.POINTER(FfnDesc), C.POINTER(GgmlTensor), C.POINTER(GgmlTensor),

@@ -10,7 +10,8 @@ the same bytes:
 * INT8 (loader/latent_loader.py:148-158): scale = absmax/127 in fp32
   (0 -> 1.0), q = clip(round_half_even(v/scale), -127, 127), fp16 scale.
 * Per-group fallback: a group whose NF4 amplitude SNR ||v|| / ||v - nf4(v)||
-  (loader/latent_loader.py:173-185) is below 10**(snr_db/20) is stored INT8.
+  (loader/latent_loader.py:173-185) is below 10**(snr_db/20) is stored INT8
+  (an all-zero group stays NF4).
 
 The nearest-level search buckets by level midpoints and then compares the
 exact fp32 distances of the neighbouring levels, which reproduces numpy's
@@ -77,7 +78,7 @@ def quantize_factor(values: torch.Tensor, snr_db: Optional[float] = 20.0) -> Gro
         deq = _levels(g.device)[codes.long()] * scale16.to(torch.float32)[:, None]
         sig = torch.linalg.vector_norm(g, dim=1)
         noise = torch.linalg.vector_norm(g - deq, dim=1).clamp_min(1e-12)
-        is_i8 = (sig / noise) < torch.tensor(10.0 ** (snr_db / 20.0), dtype=torch.float32)
+        is_i8 = ((sig / noise) < torch.tensor(10.0 ** (snr_db / 20.0), dtype=torch.float32)) & (sig > 0)
         if bool(is_i8.any()):
             gi = g[is_i8]
             s = gi.abs().amax(dim=1) / torch.tensor(127.0, dtype=torch.float32, device=g.device)

@@ -136,7 +136,8 @@ def mixed_encode(values: np.ndarray, snr_db: float = 20.0, group: int = 32) -> D
 
     Every ``group``-element group is NF4-encoded; a group whose amplitude SNR
     (reference definition) is below ``10**(snr_db/20)`` is re-encoded with the
-    reference INT8 encoder applied to that group alone.  Returns the NF4 codes
+    reference INT8 encoder applied to that group alone (an all-zero group, SNR
+    0 by that definition, stays NF4).  Returns the NF4 codes
     (packed), one fp16 scale per group (NF4 absmax or INT8 absmax/127), a bool
     mask of INT8 groups and the int8 values of every group (zeros for NF4
     groups).
@@ -145,8 +146,8 @@ def mixed_encode(values: np.ndarray, snr_db: float = 20.0, group: int = 32) -> D
     packed, scales, _ = nf4_encode(values, group)
     deq = nf4_decode(packed, scales, shape, group)
     snr = group_snr(values, deq, group)
-    is_i8 = snr < np.float32(10.0 ** (snr_db / 20.0))
     g, _ = _grouped(values, group)
+    is_i8 = (snr < np.float32(10.0 ** (snr_db / 20.0))) & np.any(g != 0, axis=1)   # an all-zero group stays NF4
     q_all = np.zeros_like(g, dtype=np.int8)
     scales = scales.copy()
     if is_i8.any():

@@ -29,6 +29,10 @@ Fixtures:
   moe.npz      a small routed MoE layer: per-expert artifacts, x, ids (with -1
                slots), weights, per-slot outputs of the reference swiglu_expert
                and the fp64 top-k combine
+  compress.npz the reference compressor's stages on two spectral matrices:
+               full singular values, choose_rank, the seeded Gaussian test
+               matrix, randomized_svd + make_factors (float A, B),
+               quantize_nf4 bytes of A and B, compress_matrix's report
 """
 
 from __future__ import annotations
@@ -145,6 +149,32 @@ def make_mixed(ll):
         HERE / "mixed.npz", values=v, nf4=np.concatenate(nf4_packed),
         scales=np.array(scales, np.float16), is_int8=np.array(is_i8),
         int8=np.concatenate(q_all), decoded=np.concatenate(decoded).reshape(v.shape))
+
+
+def make_compress(ll):
+    rng = np.random.default_rng(31)
+    out = {}
+    cases = [(256, 192, 0.9, 8, 64, 5), (192, 320, 0.999, 64, 64, 9)]   # (m, n, energy, min, max, seed)
+    for i, (m, n, energy, rmin, rmax, seed) in enumerate(cases):
+        w = _spectral(rng, m, n, 0)
+        full_s = np.linalg.svd(w, compute_uv=False)
+        rank = ll.choose_rank(full_s, energy=energy, min_rank=rmin, max_rank=rmax)
+        u, s, vt = ll.randomized_svd(w, target_rank=rank, seed=seed)
+        a, b = ll.make_factors(u, s, vt, rank)
+        ap, asc, _ = ll.quantize_nf4(a, group_size=32)
+        bp, bsc, _ = ll.quantize_nf4(b, group_size=32)
+        _, report = ll.compress_matrix(
+            name="w", matrix=w, energy=energy, min_rank=rmin, max_rank=rmax, group_size=32, int8_group_size=64,
+            error_threshold=10.0, snr_threshold=0.0, low_snr_fraction_threshold=1.0, seed=seed)
+        out.update({f"c{i}.w": w, f"c{i}.energy": np.float64(energy), f"c{i}.min_rank": np.int32(rmin),
+                    f"c{i}.max_rank": np.int32(rmax), f"c{i}.seed": np.int32(seed), f"c{i}.full_s": full_s,
+                    f"c{i}.rank": np.int32(rank), f"c{i}.a": a, f"c{i}.b": b, f"c{i}.a_nf4": ap,
+                    f"c{i}.a_scales": asc, f"c{i}.b_nf4": bp, f"c{i}.b_scales": bsc,
+                    f"c{i}.dense_error": np.float64(report.dense_relative_error),
+                    f"c{i}.quant_error": np.float64(report.quantized_relative_error),
+                    f"c{i}.retained": np.float64(report.retained_energy)})
+    out["n_cases"] = np.int32(len(cases))
+    np.savez_compressed(HERE / "compress.npz", **out)
 
 
 def make_runtime(ll, lr):
@@ -295,6 +325,7 @@ def main() -> int:
     make_nf4(ll)
     make_int8(ll)
     make_mixed(ll)
+    make_compress(ll)
     make_runtime(ll, lr)
     make_moe(ll, lr)
     make_router(args.reference)
