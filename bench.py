@@ -468,7 +468,8 @@ def run_prefill(args, cfg_id: int, dev, steps: int, warmup: int):
         "roofline_step": {"achieved": all_flops / (total * 1e-3) / 1e12,
                           "frac": all_flops / (total * 1e-3) / 1e12 / pk["bf16_tflops"], "unit": "TFLOP/s"},
         "phase_ms": {PREFILL_PHASES[i]: float(phase_ms[i]) for i in range(len(PREFILL_PHASES))},
-        "gpu_launches": steps * ((1 if ids.numel() <= 4096 else 3) + 8 + 4 + 1),
+        # routing (1 or 3), tile offsets + 6 dequant + gather, 4 GEMMs (the combine runs in G4's epilogue)
+        "gpu_launches": steps * ((1 if ids.numel() <= 4096 else 3) + 8 + 4),
         "gen_s": gen_s,
     }
 

@@ -4,7 +4,9 @@
 //   G1  T  = Xp . [A_g|A_u]           Xp: routed rows of x in expert order
 //   G2  H  = silu(T_g.B_g) * (T_u.B_u) [* w]   dual accumulator, SwiGLU epilogue
 //   G3  S  = H . A_d
-//   G4  Y  = S . B_d                   (per routed row; then the top-k combine)
+//   G4  Y  = S . B_d                   the epilogue adds w * Y into the
+//                                      token's output row (red.add on an output
+//                                      zeroed before G1), or stores Y per slot
 // Factors are first dequantized (NF4 / INT8, bit-exact fp32 values rounded
 // once to f16) into K-major f16 copies in the workspace; activations between
 // GEMMs are f16.  f16 rather than bf16 operands: a numpy emulation of this
@@ -157,8 +159,9 @@ struct GemmArgs {
     const void *weights;
     int w_type;
     uint32_t flags;
-    int per_slot_d;            // kModeF32 with OUT_PER_SLOT: write out[slot][col], row length d
-    float *out_slot;
+    int per_slot_d;            // kModeF32: row length d of out_slot
+    float *out_slot;           // kModeF32: the op's output; [slot][d] with OUT_PER_SLOT, else [token][d] += w * y
+    int top_k;
     uint32_t *err;
 };
 
@@ -361,15 +364,27 @@ __global__ void __launch_bounds__(256, 1) k_pf_gemm(const __grid_constant__ CUte
                                 for (int t = 0; t < 8; ++t) hv[t] = __float2half_rn(__uint_as_float(v[j + t]));
                                 if (n0 + c + j + 8 <= g.N) *reinterpret_cast<uint4 *>(o + j) = *reinterpret_cast<uint4 *>(hv);
                             }
-                        } else {
-                            float *o = g.out_slot ? g.out_slot + (int64_t)g.order[grow] * g.per_slot_d + n0 + c
-                                                  : reinterpret_cast<float *>(g.out) + grow * g.ldo + n0 + c;
+                        } else if (g.flags & LATENT_FLAG_OUT_PER_SLOT) {
+                            float *o = g.out_slot + (int64_t)g.order[grow] * g.per_slot_d + n0 + c;
 #pragma unroll
                             for (int j = 0; j < 32; j += 4) {
                                 if (n0 + c + j + 4 <= g.N)
                                     *reinterpret_cast<float4 *>(o + j) =
                                         make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
                                                     __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                            }
+                        } else {  // the top-k combine: out[token] += w * y (out zeroed before G1)
+                            const int slot = g.order[grow];
+                            const float w = (g.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN)
+                                                ? 1.f : load_weight(g.weights, g.w_type, slot);
+                            float *o = g.out_slot + (int64_t)(slot / g.top_k) * g.per_slot_d + n0 + c;
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4) {
+                                if (n0 + c + j + 4 <= g.N)
+                                    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(o + j),
+                                                 "f"(w * __uint_as_float(v[j])), "f"(w * __uint_as_float(v[j + 1])),
+                                                 "f"(w * __uint_as_float(v[j + 2])), "f"(w * __uint_as_float(v[j + 3]))
+                                                 : "memory");
                             }
                         }
                     }
@@ -449,7 +464,7 @@ size_t al(size_t x) { return (x + 255) / 256 * 256; }
 size_t prefill_scratch_bytes(const DecodeArgs &a) {
     const size_t E = a.E, R = a.R, d = a.d, f = a.f, r = a.r;
     return al((E + 1) * 4) + al(R * d * 2) + al(E * 2 * r * d * 2) + 2 * al(E * f * r * 2) + al(E * r * f * 2) +
-           al(E * d * r * 2) + al(R * 2 * r * 2) + al(R * f * 2) + al(R * r * 2) + al(R * d * 4);
+           al(E * d * r * 2) + al(R * 2 * r * 2) + al(R * f * 2) + al(R * r * 2);
 }
 
 cudaError_t launch_prefill(const DecodeArgs &a, void *scratch, cudaStream_t s, Marks *marks) {
@@ -466,11 +481,12 @@ cudaError_t launch_prefill(const DecodeArgs &a, void *scratch, cudaStream_t s, M
     __half *tb = reinterpret_cast<__half *>(take(R * 2 * r * 2));
     __half *hb = reinterpret_cast<__half *>(take(R * f * 2));
     __half *sb = reinterpret_cast<__half *>(take(R * r * 2));
-    float *yb = reinterpret_cast<float *>(take(R * d * 4));
     cudaError_t err;
     Marks none;
     Marks &mk = marks ? *marks : none;
 
+    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
+    if (!per_slot && (err = cudaMemsetAsync(a.out, 0, (size_t)a.T * d * sizeof(float), s)) != cudaSuccess) return err;
     k_pf_mtiles<<<1, 1024, 0, s>>>(a.rt.counts, a.E, mtile_off);
     if ((err = cudaGetLastError()) != cudaSuccess) return err;
     if ((err = launch_dequant_t(a.gate_a, a.E, w1t, (int64_t)2 * r * d, 0, s)) != cudaSuccess) return err;
@@ -512,15 +528,15 @@ cudaError_t launch_prefill(const DecodeArgs &a, void *scratch, cudaStream_t s, M
     g.K = a.f; g.N = a.r; g.ldo = a.r; g.out = sb; g.a_koff2 = 0;
     if ((err = launch_gemm<kModeF16>(mH, mAd, mAd, g, s)) != cudaSuccess) return err;
     mk.mark(s);
-    const bool per_slot = a.flags & LATENT_FLAG_OUT_PER_SLOT;
-    g.K = a.r; g.N = a.d; g.ldo = a.d; g.out = yb;
-    g.out_slot = per_slot ? a.out : nullptr;
+    g.K = a.r; g.N = a.d; g.ldo = a.d; g.out = nullptr;
+    g.out_slot = a.out;
     g.per_slot_d = a.d;
+    g.top_k = a.k;
     if ((err = launch_gemm<kModeF32>(mS, mBd, mBd, g, s)) != cudaSuccess) return err;
     mk.mark(s);
-    DecodeArgs c = a;
-    c.y = yb;
-    err = launch_combine(c, s);
+    // per-slot output: the rows of skipped slots are zeroed here; the combined
+    // output was summed by G4's epilogue
+    if (per_slot) err = launch_combine(a, s);
     mk.mark(s);
     return err;
 }
