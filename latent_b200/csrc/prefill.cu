@@ -92,16 +92,38 @@ __global__ void __launch_bounds__(256) k_pf_dequant_t(latent_qmatrix m, __half *
     }
 }
 
-// Routed rows of x in expert order, converted to f16: xp[p] = f16(x[order[p] / k]).
+// Routed rows of x in expert order, converted to f16: xp[p] = f16(x[order[p] / k]); 8 elements per thread.
 template <int XT>
 __global__ void __launch_bounds__(256) k_pf_gather(const void *x, const int32_t *order, const int32_t *offsets, int E,
                                                    int k, int d, __half *xp) {
     const int p = blockIdx.x;
     if (p >= __ldg(offsets + E)) return;
     const int64_t src = (int64_t)(__ldg(order + p) / k) * d;
-    for (int c = threadIdx.x * 2; c < d; c += 512) {
-        const float v0 = load_act<XT>(x, src + c), v1 = load_act<XT>(x, src + c + 1);
-        reinterpret_cast<__half2 *>(xp + (int64_t)p * d)[c >> 1] = __floats2half2_rn(v0, v1);
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0) {  // x only element-aligned: scalar loads
+        for (int c = threadIdx.x * 2; c < d; c += blockDim.x * 2) {
+            const float v0 = load_act<XT>(x, src + c), v1 = load_act<XT>(x, src + c + 1);
+            reinterpret_cast<__half2 *>(xp + (int64_t)p * d)[c >> 1] = __floats2half2_rn(v0, v1);
+        }
+        return;
+    }
+    for (int c = threadIdx.x * 8; c < d; c += blockDim.x * 8) {
+        __align__(16) __half hv[8];
+        if constexpr (XT == LATENT_TYPE_F16) {
+            *reinterpret_cast<uint4 *>(hv) = __ldg(reinterpret_cast<const uint4 *>(static_cast<const __half *>(x) + src + c));
+        } else if constexpr (XT == LATENT_TYPE_BF16) {
+            __align__(16) __nv_bfloat16 bv[8];
+            *reinterpret_cast<uint4 *>(bv) =
+                __ldg(reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(x) + src + c));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) hv[j] = __float2half_rn(__bfloat162float(bv[j]));
+        } else {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(x) + src + c));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(x) + src + c) + 1);
+            const float f8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) hv[j] = __float2half_rn(f8[j]);
+        }
+        *reinterpret_cast<uint4 *>(xp + (int64_t)p * d + c) = *reinterpret_cast<const uint4 *>(hv);
     }
 }
 
