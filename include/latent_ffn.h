@@ -402,10 +402,20 @@ LATENT_API int latent_pack_tiles(const uint8_t *codes, const uint16_t *scales, i
  * then holds a NaN keeps all top_k slots with NaN weights, as the reference
  * does.  Stream-ordered,
  * allocates nothing; ids/weights feed latent_expert_ffn_forward directly. */
-enum { LATENT_ROUTER_RENORMALIZE = 1u << 0 };
+enum { LATENT_ROUTER_RENORMALIZE = 1u << 0, LATENT_ROUTER_SOFTMAX = 1u << 1 };
 LATENT_API int latent_router_topk(const float *scores, int32_t n_tokens, int32_t n_expert, int32_t top_k,
                                   double threshold, uint32_t flags, int32_t *ids, float *weights, int32_t *n_kept,
                                   struct CUstream_st *stream);
+
+/* The router in one kernel: latent_router_topk, plus LATENT_ROUTER_SOFTMAX
+ * (scores are logits: p = exp(l - max) / sum in fp32 per token, the maximum
+ * and the sum by warp reductions; the selection then runs on p) and
+ * expert_counts (optional, [n_expert] int32, zeroed by the call): the kept
+ * slots per expert, the histogram the fused op's routing builds.  NaN
+ * logits give NaN probabilities. */
+LATENT_API int latent_router_route(const float *scores, int32_t n_tokens, int32_t n_expert, int32_t top_k,
+                                   double threshold, uint32_t flags, int32_t *ids, float *weights, int32_t *n_kept,
+                                   int32_t *expert_counts, struct CUstream_st *stream);
 
 #ifdef __cplusplus
 }

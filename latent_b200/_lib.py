@@ -25,6 +25,7 @@ TYPE_F32, TYPE_F16, TYPE_BF16 = 0, 1, 2
 FLAG_WEIGHT_BEFORE_DOWN = 1 << 0
 FLAG_OUT_PER_SLOT = 1 << 1
 ROUTER_RENORMALIZE = 1 << 0
+ROUTER_SOFTMAX = 1 << 1
 PATH_AUTO, PATH_DECODE, PATH_PREFILL = 0, 1, 2
 
 # Every entry point the header declares, with (restype, argtypes).
@@ -169,6 +170,8 @@ EXPORTS.update({
                                           C.c_void_p]),
     "latent_router_topk": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_double, C.c_uint32,
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "latent_router_route": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_double, C.c_uint32,
+                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "latent_pack_tiles": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p,
                                     C.c_void_p]),
 })

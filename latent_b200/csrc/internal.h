@@ -136,7 +136,7 @@ cudaError_t launch_ep_combine_fixed(const EpArgs &a, const int32_t *pos, int wor
 cudaError_t launch_dequant(const latent_qmatrix &m, int expert, float *out, cudaStream_t s);
 cudaError_t launch_silu(const float *x, float *y, int64_t n, cudaStream_t s);
 cudaError_t launch_router_topk(const float *scores, int T, int E, int k, double threshold, bool renorm, int *ids,
-                               float *weights, int *n_kept, cudaStream_t s);
+                               float *weights, int *n_kept, bool softmax, int *counts, cudaStream_t s);
 cudaError_t launch_pack_tiles(const uint8_t *codes, const uint16_t *scales, int n_expert, int64_t rows, int64_t cols,
                               uint8_t *dcodes, uint16_t *dscales, cudaStream_t s);
 

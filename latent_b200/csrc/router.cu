@@ -59,135 +59,200 @@ __device__ __forceinline__ unsigned score_key(float v) {
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-template <int NPL>
+// With SOFTMAX the row holds logits: p = exp(l - max) / sum in fp32 (the
+// maximum and the sum by warp reductions), then the same selection.  With
+// counts != NULL the kept slots are counted per expert (a shared-memory
+// histogram per block, added to counts with one atomic per expert).
+template <int NPL, bool SOFTMAX>
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router_topk(const float *__restrict__ scores, int T, int E,
                                                                     int k, double threshold, bool renorm,
                                                                     int *__restrict__ ids, float *__restrict__ weights,
-                                                                    int *__restrict__ n_kept) {
+                                                                    int *__restrict__ n_kept, int *__restrict__ counts) {
     __shared__ float s_val[kRouterWarps][kMaxRouterTopK];
     __shared__ int s_idx[kRouterWarps][kMaxRouterTopK];
+    __shared__ int s_hist[kMaxRouterExperts];
     const unsigned full = 0xffffffffu;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * kRouterWarps + warp;
-    if (t >= T) return;
-    const float *row = scores + (size_t)t * E;
-    float v[NPL];
-    unsigned key[NPL];    // 0: padding or already selected; 1: NaN
-#pragma unroll
-    for (int j = 0; j < NPL; ++j) {
-        const int e = j * 32 + lane;
-        v[j] = e < E ? __ldg(row + e) : 0.f;
-        key[j] = e >= E ? 0u : v[j] != v[j] ? 1u : score_key(v[j]);
+    if (counts) {
+        for (int i = threadIdx.x; i < E; i += blockDim.x) s_hist[i] = 0;
+        __syncthreads();
     }
-    // each lane's best remaining element (lowest index among equal scores)
-    unsigned lkey = 0;
-    int lj = 0;
-    auto rescan = [&]() {
-        lkey = 0;
-        lj = 0;
+    const int t = blockIdx.x * kRouterWarps + warp;
+    if (t < T) {
+        const float *row = scores + (size_t)t * E;
+        float v[NPL];
+        unsigned key[NPL];    // 0: padding or already selected; 1: NaN
 #pragma unroll
         for (int j = 0; j < NPL; ++j) {
-            if (key[j] > lkey) {
-                lkey = key[j];
-                lj = j;
+            const int e = j * 32 + lane;
+            v[j] = e < E ? __ldg(row + e) : 0.f;
+        }
+        if constexpr (SOFTMAX) {
+            float m = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < NPL; ++j)
+                if (j * 32 + lane < E) m = fmaxf(m, v[j]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(full, m, o));
+            float sum = 0.f;
+#pragma unroll
+            for (int j = 0; j < NPL; ++j) {
+                v[j] = j * 32 + lane < E ? expf(__fsub_rn(v[j], m)) : 0.f;
+                sum = __fadd_rn(sum, v[j]);
             }
-        }
-    };
-    auto value_at = [&](int jj) {
-        float x = v[0];
 #pragma unroll
-        for (int j = 1; j < NPL; ++j) x = jj == j ? v[j] : x;
-        return x;
-    };
-    rescan();
-    for (int r = 0; r < k; ++r) {
-        const unsigned m = __reduce_max_sync(full, lkey);
-        const unsigned win = __reduce_min_sync(full, lkey == m ? (unsigned)(lj * 32 + lane) : 0xffffffffu);
-        const bool none = m == 0u;
-        // the score back from its key; a zero or NaN score takes the winner's own bits (the sign of -0, the payload)
-        float val = __uint_as_float((m & 0x80000000u) ? (m & 0x7fffffffu) : ~m);
-        if (m == 0x80000000u || m == 1u) val = __shfl_sync(full, value_at(lj), (int)(win & 31u));
-        if (!none && lane == (int)(win & 31u)) {
+            for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(full, sum, o));
 #pragma unroll
-            for (int j = 0; j < NPL; ++j) key[j] = j == lj ? 0u : key[j];
-            rescan();
+            for (int j = 0; j < NPL; ++j) v[j] = __fdiv_rn(v[j], sum);
         }
-        if (lane == 0) {
-            s_val[warp][r] = none ? 0.f : val;
-            s_idx[warp][r] = none ? -1 : (int)win;
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) {
+            const int e = j * 32 + lane;
+            key[j] = e >= E ? 0u : v[j] != v[j] ? 1u : score_key(v[j]);
         }
-    }
-    __syncwarp();
-    const float my_val = lane < k ? s_val[warp][lane] : 0.f;   // lane i writes slot i
-    const int my_idx = lane < k ? s_idx[warp][lane] : -1;
-    // adaptive_topk_inclusive (loader/adaptive_topk.py:46-56), by lane 0 in slot order
-    int n = k;
-    float cum = 0.f;
-    if (lane == 0) {
-        const float *sv = s_val[warp];
-        const float total = f32_sum(sv, k);
-        if (total <= 0.f) {
-            n = 0;
-        } else {
-            const float target = __double2float_rn(threshold * (double)total);
-            for (int i = 0; i < k; ++i) {
-                const float next = __fadd_rn(cum, sv[i]);
-                if (next > target) {
-                    n = i;
-                    break;
+        // each lane's best remaining element (lowest index among equal scores)
+        unsigned lkey = 0;
+        int lj = 0;
+        auto rescan = [&]() {
+            lkey = 0;
+            lj = 0;
+#pragma unroll
+            for (int j = 0; j < NPL; ++j) {
+                if (key[j] > lkey) {
+                    lkey = key[j];
+                    lj = j;
                 }
-                cum = next;
+            }
+        };
+        auto value_at = [&](int jj) {
+            float x = v[0];
+#pragma unroll
+            for (int j = 1; j < NPL; ++j) x = jj == j ? v[j] : x;
+            return x;
+        };
+        rescan();
+        for (int r = 0; r < k; ++r) {
+            const unsigned m = __reduce_max_sync(full, lkey);
+            const unsigned win = __reduce_min_sync(full, lkey == m ? (unsigned)(lj * 32 + lane) : 0xffffffffu);
+            const bool none = m == 0u;
+            // the score back from its key; a zero or NaN score takes the winner's own bits (the sign of -0, the payload)
+            float val = __uint_as_float((m & 0x80000000u) ? (m & 0x7fffffffu) : ~m);
+            if (m == 0x80000000u || m == 1u) val = __shfl_sync(full, value_at(lj), (int)(win & 31u));
+            if (!none && lane == (int)(win & 31u)) {
+#pragma unroll
+                for (int j = 0; j < NPL; ++j) key[j] = j == lj ? 0u : key[j];
+                rescan();
+            }
+            if (lane == 0) {
+                s_val[warp][r] = none ? 0.f : val;
+                s_idx[warp][r] = none ? -1 : (int)win;
             }
         }
+        __syncwarp();
+        const float my_val = lane < k ? s_val[warp][lane] : 0.f;   // lane i writes slot i
+        const int my_idx = lane < k ? s_idx[warp][lane] : -1;
+        // adaptive_topk_inclusive (loader/adaptive_topk.py:46-56), by lane 0 in slot order
+        int n = k;
+        float cum = 0.f;
+        if (lane == 0) {
+            const float *sv = s_val[warp];
+            const float total = f32_sum(sv, k);
+            if (total <= 0.f) {
+                n = 0;
+            } else {
+                const float target = __double2float_rn(threshold * (double)total);
+                for (int i = 0; i < k; ++i) {
+                    const float next = __fadd_rn(cum, sv[i]);
+                    if (next > target) {
+                        n = i;
+                        break;
+                    }
+                    cum = next;
+                }
+            }
+        }
+        n = __shfl_sync(full, n, 0);
+        cum = __shfl_sync(full, cum, 0);
+        if (lane < k) {
+            const bool keep = lane < n && my_idx >= 0;
+            ids[(size_t)t * k + lane] = keep ? my_idx : -1;
+            weights[(size_t)t * k + lane] = keep ? (renorm ? __fdiv_rn(my_val, cum) : my_val) : 0.f;
+            if (counts && keep) atomicAdd(&s_hist[my_idx], 1);
+        }
+        if (lane == 0 && n_kept) n_kept[t] = n;
     }
-    n = __shfl_sync(full, n, 0);
-    cum = __shfl_sync(full, cum, 0);
-    if (lane < k) {
-        const bool keep = lane < n && my_idx >= 0;
-        ids[(size_t)t * k + lane] = keep ? my_idx : -1;
-        weights[(size_t)t * k + lane] = keep ? (renorm ? __fdiv_rn(my_val, cum) : my_val) : 0.f;
+    if (counts) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < E; i += blockDim.x)
+            if (s_hist[i]) atomicAdd(counts + i, s_hist[i]);
     }
-    if (lane == 0 && n_kept) n_kept[t] = n;
 }
 
 template <int NPL>
 void launch(const float *scores, int T, int E, int k, double threshold, bool renorm, int *ids, float *w, int *nk,
-            cudaStream_t s) {
+            bool softmax, int *counts, cudaStream_t s) {
     const int blocks = (T + kRouterWarps - 1) / kRouterWarps;
-    k_router_topk<NPL><<<blocks, kRouterWarps * 32, 0, s>>>(scores, T, E, k, threshold, renorm, ids, w, nk);
+    if (softmax)
+        k_router_topk<NPL, true><<<blocks, kRouterWarps * 32, 0, s>>>(scores, T, E, k, threshold, renorm, ids, w, nk,
+                                                                      counts);
+    else
+        k_router_topk<NPL, false><<<blocks, kRouterWarps * 32, 0, s>>>(scores, T, E, k, threshold, renorm, ids, w, nk,
+                                                                       counts);
 }
 
 }  // namespace
 
 cudaError_t launch_router_topk(const float *scores, int T, int E, int k, double threshold, bool renorm, int *ids,
-                               float *weights, int *n_kept, cudaStream_t s) {
+                               float *weights, int *n_kept, bool softmax, int *counts, cudaStream_t s) {
+    if (counts) {
+        const cudaError_t e = cudaMemsetAsync(counts, 0, (size_t)E * sizeof(int), s);
+        if (e != cudaSuccess) return e;
+    }
     if (T == 0) return cudaSuccess;
-    if (E <= 32) launch<1>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
-    else if (E <= 64) launch<2>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
-    else if (E <= 128) launch<4>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
-    else if (E <= 256) launch<8>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
-    else if (E <= 512) launch<16>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
-    else launch<32>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, s);
+    if (E <= 32) launch<1>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, softmax, counts, s);
+    else if (E <= 64) launch<2>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, softmax, counts, s);
+    else if (E <= 128) launch<4>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, softmax, counts, s);
+    else if (E <= 256) launch<8>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, softmax, counts, s);
+    else if (E <= 512) launch<16>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, softmax, counts, s);
+    else launch<32>(scores, T, E, k, threshold, renorm, ids, weights, n_kept, softmax, counts, s);
     return cudaGetLastError();
 }
 
 }  // namespace latent
 
-extern "C" LATENT_API int latent_router_topk(const float *scores, int32_t n_tokens, int32_t n_expert, int32_t top_k,
-                                             double threshold, uint32_t flags, int32_t *ids, float *weights,
-                                             int32_t *n_kept, CUstream_st *stream) {
+namespace {
+
+int router_entry(const float *scores, int32_t n_tokens, int32_t n_expert, int32_t top_k, double threshold,
+                 uint32_t flags, int32_t *ids, float *weights, int32_t *n_kept, int32_t *counts, CUstream_st *stream) {
     using namespace latent;
     if (n_tokens < 0 || n_expert < 1 || top_k < 1 || top_k > n_expert) return LATENT_ERR_SHAPE;
     if (!(threshold > 0.0 && threshold <= 1.0)) return LATENT_ERR_INVALID;
-    if (flags & ~(uint32_t)LATENT_ROUTER_RENORMALIZE) return LATENT_ERR_INVALID;
+    if (flags & ~(uint32_t)(LATENT_ROUTER_RENORMALIZE | LATENT_ROUTER_SOFTMAX)) return LATENT_ERR_INVALID;
     if (n_expert > kMaxRouterExperts || top_k > kMaxRouterTopK) return LATENT_ERR_UNSUPPORTED;
-    if (n_tokens == 0) return LATENT_OK;
-    if (!scores || !ids || !weights) return LATENT_ERR_INVALID;
+    if (n_tokens > 0 && (!scores || !ids || !weights)) return LATENT_ERR_INVALID;
     if (!router_aligned(scores, 4) || !router_aligned(ids, 4) || !router_aligned(weights, 4) ||
-        (n_kept && !router_aligned(n_kept, 4)))
+        (n_kept && !router_aligned(n_kept, 4)) || (counts && !router_aligned(counts, 4)))
         return LATENT_ERR_ALIGN;
+    if (n_tokens == 0 && !counts) return LATENT_OK;
     const cudaError_t e = launch_router_topk(scores, n_tokens, n_expert, top_k, threshold,
                                              (flags & LATENT_ROUTER_RENORMALIZE) != 0, ids, weights, n_kept,
+                                             (flags & LATENT_ROUTER_SOFTMAX) != 0, counts,
                                              reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? LATENT_OK : LATENT_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" LATENT_API int latent_router_topk(const float *scores, int32_t n_tokens, int32_t n_expert, int32_t top_k,
+                                             double threshold, uint32_t flags, int32_t *ids, float *weights,
+                                             int32_t *n_kept, CUstream_st *stream) {
+    if (flags & LATENT_ROUTER_SOFTMAX) return LATENT_ERR_INVALID;  // scores are probabilities here
+    return router_entry(scores, n_tokens, n_expert, top_k, threshold, flags, ids, weights, n_kept, nullptr, stream);
+}
+
+extern "C" LATENT_API int latent_router_route(const float *scores, int32_t n_tokens, int32_t n_expert, int32_t top_k,
+                                              double threshold, uint32_t flags, int32_t *ids, float *weights,
+                                              int32_t *n_kept, int32_t *expert_counts, CUstream_st *stream) {
+    return router_entry(scores, n_tokens, n_expert, top_k, threshold, flags, ids, weights, n_kept, expert_counts,
+                        stream);
 }

@@ -358,7 +358,8 @@ def _to_dev(a, dev, dtype=None):
 _OPS: Dict[int, ExpertFFN] = {}
 
 
-def router_topk(scores: torch.Tensor, top_k: int, threshold: float = 0.95, renormalize: bool = True):
+def router_topk(scores: torch.Tensor, top_k: int, threshold: float = 0.95, renormalize: bool = True,
+                logits: bool = False, expert_counts: bool = False):
     """Adaptive top-k routing on the device (latent_router_topk).
 
     scores: [T, E] fp32 router scores on a CUDA device.  Returns (ids [T, k]
@@ -367,6 +368,9 @@ def router_topk(scores: torch.Tensor, top_k: int, threshold: float = 0.95, renor
     threshold rule dropped to id -1 / weight 0 (loader/adaptive_topk.py:29-90),
     kept weights renormalised to sum to 1 unless ``renormalize`` is False.
     The ids and weights feed ``ExpertFFN`` / ``moe_expert_ffn`` directly.
+    With ``logits`` the scores are router logits and the softmax runs in the
+    same kernel (latent_router_route); with ``expert_counts`` a fourth
+    result holds the kept slots per expert [E] int32.
     Raises ValueError where the reference does (threshold outside (0, 1],
     top_k > n_experts, scores not 2-D)."""
     if not torch.is_tensor(scores) or scores.device.type != "cuda":
@@ -384,11 +388,13 @@ def router_topk(scores: torch.Tensor, top_k: int, threshold: float = 0.95, renor
     ids = torch.empty((T, top_k), dtype=torch.int32, device=s.device)
     w = torch.empty((T, top_k), dtype=torch.float32, device=s.device)
     n_kept = torch.empty(T, dtype=torch.int32, device=s.device)
-    flags = _lib.ROUTER_RENORMALIZE if renormalize else 0
-    _lib.check(_lib.lib().latent_router_topk(s.data_ptr(), T, E, top_k, float(threshold), flags, ids.data_ptr(),
-                                             w.data_ptr(), n_kept.data_ptr(), _stream_ptr(s.device)),
-               "latent_router_topk")
-    return ids, w, n_kept
+    flags = (_lib.ROUTER_RENORMALIZE if renormalize else 0) | (_lib.ROUTER_SOFTMAX if logits else 0)
+    counts = torch.empty(E, dtype=torch.int32, device=s.device) if expert_counts else None
+    _lib.check(_lib.lib().latent_router_route(s.data_ptr(), T, E, top_k, float(threshold), flags, ids.data_ptr(),
+                                              w.data_ptr(), n_kept.data_ptr(),
+                                              counts.data_ptr() if counts is not None else None,
+                                              _stream_ptr(s.device)), "latent_router_route")
+    return (ids, w, n_kept, counts) if expert_counts else (ids, w, n_kept)
 
 
 def moe_expert_ffn(x, ids, weights, experts: ExpertSet, weight_before_down: bool = False,

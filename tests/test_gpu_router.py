@@ -108,3 +108,36 @@ def test_router_feeds_the_fused_op(cuda):
     ids_o, w_o, _ = O.router_topk(scores, 2, 0.6)
     ref = O.moe_forward(x, ids_o, w_o, pairs)
     assert O.rel_l2(ref, y.cpu().numpy()) <= 1e-5
+
+
+@pytest.mark.parametrize("T,E,k,th", [(4096, 256, 8, 0.95), (333, 64, 6, 0.8), (50, 1024, 32, 0.9)])
+def test_fused_softmax_router_and_histogram(cuda, T, E, k, th):
+    """latent_router_route with logits: the softmax (fp32, max-subtracted) runs
+    in the selection kernel.  Against the oracle on numpy's float32 softmax of
+    the same logits: ids and kept counts equal wherever no two of a token's
+    probabilities (or a running sum and the threshold target) are within
+    1e-5 relative of each other; weights within 1e-6; the per-expert counts
+    equal the histogram of the kept ids."""
+    rng = np.random.default_rng(T + E)
+    logits = (rng.standard_normal((T, E)) * 2.0).astype(np.float32)
+    ids, w, nk, counts = router_topk(torch.from_numpy(logits).cuda(), k, th, logits=True, expert_counts=True)
+    ids, w, nk, counts = ids.cpu().numpy(), w.cpu().numpy(), nk.cpu().numpy(), counts.cpu().numpy()
+    p = np.exp(logits - logits.max(axis=1, keepdims=True))
+    p = (p / p.sum(axis=1, keepdims=True)).astype(np.float32)
+    ids_o, w_o, nk_o = O.router_topk(p, k, th)
+    top = -np.sort(-p, axis=1)[:, :k + 1]
+    close = (np.abs(np.diff(top, axis=1)) <= 1e-5 * top[:, 1:]).any(axis=1)
+    tot = top[:, :k].sum(axis=1, dtype=np.float32)
+    cum = np.cumsum(top[:, :k], axis=1)
+    close |= (np.abs(cum - th * tot[:, None]) <= 1e-5 * tot[:, None]).any(axis=1)
+    ok = ~close
+    assert ok.mean() > 0.9
+    assert np.array_equal(ids[ok], ids_o[ok]) and np.array_equal(nk[ok], nk_o[ok])
+    assert np.allclose(w[ok], w_o[ok], rtol=1e-6, atol=1e-7)
+    want = np.bincount(ids[ids >= 0].ravel(), minlength=E)
+    assert np.array_equal(counts, want)
+    # probabilities in, through the same entry point: bit-exact with latent_router_topk
+    ids2, w2, nk2 = router_topk(torch.from_numpy(p).cuda(), k, th)
+    ids3, w3, nk3 = O.router_topk(p, k, th)
+    assert np.array_equal(ids2.cpu().numpy(), ids3) and np.array_equal(nk2.cpu().numpy(), nk3)
+
