@@ -35,6 +35,8 @@ import os
 _NCPU = os.cpu_count() or 1
 for _v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
     os.environ.setdefault(_v, str(_NCPU))
+# NCCL's own messages (e.g. its version line) go to stderr: stdout carries the one JSON line
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 import argparse
 import datetime

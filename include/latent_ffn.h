@@ -199,6 +199,21 @@ LATENT_API int latent_ep_pack_fixed(const latent_ep_desc *desc, int32_t world, i
 LATENT_API int latent_ep_combine_fixed(const latent_ep_desc *desc, int32_t world, int32_t cap, const float *y_rows,
                                        float *out, struct CUstream_st *stream);
 
+/* The fixed-capacity blocks with rows and metadata in one buffer, so that
+ * one all-to-all carries both: block g (world blocks of equal size) =
+ * [cap rows of x (x's type)][cap {global expert id, weight bits} int32 pairs,
+ * padded to 16 bytes].  send_buf == NULL: only *bytes_needed is written.
+ * latent_ep_unpack_fixed turns the received buffer into the local op's
+ * inputs: x_out[world*cap][d], ids_out[world*cap] (id - expert_base for the
+ * n_local local experts, -1 for unused rows; an id outside them records
+ * LATENT_ERR_EXPERT_ID's bit in *err_word when given) and w_out (the weight
+ * with LATENT_FLAG_WEIGHT_BEFORE_DOWN, else 1). */
+LATENT_API int latent_ep_pack_fixed_merged(const latent_ep_desc *desc, int32_t world, int32_t cap, void *send_buf,
+                                           size_t buf_bytes, size_t *bytes_needed, struct CUstream_st *stream);
+LATENT_API int latent_ep_unpack_fixed(const void *recv_buf, int32_t world, int32_t cap, int32_t n_embd, int32_t x_type,
+                                      int32_t expert_base, int32_t n_local, uint32_t flags, void *x_out,
+                                      int32_t *ids_out, float *w_out, uint32_t *err_word, struct CUstream_st *stream);
+
 /* Dense-fallback experts (reference: the compressor keeps a dense fp16
  * copy `<name>.dense_fallback` of a matrix whose factors miss its error
  * threshold, loader/latent_loader.py:262-265; the dense forward is

@@ -143,6 +143,11 @@ EXPORTS.update({
     "latent_ep_dispatch": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_ep_combine": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
     "latent_ep_check": (C.c_int, [C.POINTER(EpDesc), C.c_void_p]),
+    "latent_ep_pack_fixed_merged": (C.c_int, [C.POINTER(EpDesc), C.c_int32, C.c_int32, C.c_void_p, C.c_size_t,
+                                              C.POINTER(C.c_size_t), C.c_void_p]),
+    "latent_ep_unpack_fixed": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                         C.c_int32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_void_p]),
     "latent_dense_workspace_size": (C.c_int, [C.POINTER(DenseDesc), C.POINTER(C.c_size_t)]),
     "latent_quantize_groups": (C.c_int, [C.c_void_p, C.c_int64, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_void_p, C.c_void_p, C.c_void_p]),

@@ -402,7 +402,43 @@ extern "C" LATENT_API int latent_ep_pack_fixed(const latent_ep_desc *desc, int32
         return cuda_status(cudaMemsetAsync(send_meta, 0xff, (size_t)world * cap * 8, s));
     if (!desc->send_x || !desc->send_expert || !desc->send_weight) return LATENT_ERR_INVALID;
     if (!aligned(desc->send_x, 16)) return LATENT_ERR_ALIGN;
-    return cuda_status(launch_ep_pack_fixed(ep_args(desc), world, cap, send_rows, send_meta, s));
+    return cuda_status(launch_ep_pack_fixed(ep_args(desc), world, cap, send_rows, send_meta, false, s));
+}
+
+extern "C" LATENT_API int latent_ep_pack_fixed_merged(const latent_ep_desc *desc, int32_t world, int32_t cap,
+                                                      void *send_buf, size_t buf_bytes, size_t *bytes_needed,
+                                                      CUstream_st *stream) {
+    int st = ep_fixed_check(desc, world, cap);
+    if (st) return st;
+    const int es = desc->x_type == LATENT_TYPE_F32 ? 4 : 2;
+    const size_t need = (size_t)world * ep_merged_block_bytes(cap, desc->n_embd, es);
+    if (bytes_needed) *bytes_needed = need;
+    if (!send_buf) return LATENT_OK;
+    if (buf_bytes < need) return LATENT_ERR_WORKSPACE;
+    if (!aligned(send_buf, 16)) return LATENT_ERR_ALIGN;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (desc->n_tokens == 0)   // nothing routed: every row unused (id -1)
+        return cuda_status(cudaMemsetAsync(send_buf, 0xff, need, s));
+    if (!desc->send_x || !desc->send_expert || !desc->send_weight) return LATENT_ERR_INVALID;
+    if (!aligned(desc->send_x, 16)) return LATENT_ERR_ALIGN;
+    return cuda_status(launch_ep_pack_fixed(ep_args(desc), world, cap, send_buf, nullptr, true, s));
+}
+
+extern "C" LATENT_API int latent_ep_unpack_fixed(const void *recv_buf, int32_t world, int32_t cap, int32_t n_embd,
+                                                 int32_t x_type, int32_t expert_base, int32_t n_local, uint32_t flags,
+                                                 void *x_out, int32_t *ids_out, float *w_out, uint32_t *err_word,
+                                                 CUstream_st *stream) {
+    if (world < 1 || cap < 1 || (int64_t)world * cap > (int64_t)1 << 30) return LATENT_ERR_SHAPE;
+    if (n_embd < 32 || n_embd % 32 || n_local < 1 || expert_base < 0) return LATENT_ERR_SHAPE;
+    if (x_type != LATENT_TYPE_F32 && x_type != LATENT_TYPE_F16 && x_type != LATENT_TYPE_BF16) return LATENT_ERR_DTYPE;
+    if (flags & ~(uint32_t)LATENT_FLAG_WEIGHT_BEFORE_DOWN) return LATENT_ERR_INVALID;
+    if (!recv_buf || !x_out || !ids_out || !w_out) return LATENT_ERR_INVALID;
+    if (!aligned(recv_buf, 16) || !aligned(x_out, 16) || !aligned(ids_out, 4) || !aligned(w_out, 4))
+        return LATENT_ERR_ALIGN;
+    const int es = x_type == LATENT_TYPE_F32 ? 4 : 2;
+    return cuda_status(launch_ep_unpack_fixed(recv_buf, world, cap, n_embd, es, expert_base, n_local,
+                                              (flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN) != 0, x_out, ids_out, w_out,
+                                              err_word, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 extern "C" LATENT_API int latent_ep_combine_fixed(const latent_ep_desc *desc, int32_t world, int32_t cap,

@@ -129,7 +129,11 @@ struct EpArgs {
 };
 
 cudaError_t launch_ep_gather(const EpArgs &a, cudaStream_t s);
-cudaError_t launch_ep_pack_fixed(const EpArgs &a, int world, int cap, void *rows, int32_t *meta, cudaStream_t s);
+cudaError_t launch_ep_pack_fixed(const EpArgs &a, int world, int cap, void *rows, int32_t *meta, bool merged,
+                                 cudaStream_t s);
+size_t ep_merged_block_bytes(int cap, int d, int es);
+cudaError_t launch_ep_unpack_fixed(const void *buf, int world, int cap, int d, int es, int base, int n_local, bool wbd,
+                                   void *x_out, int32_t *ids_out, float *w_out, uint32_t *err, cudaStream_t s);
 cudaError_t launch_ep_combine_fixed(const EpArgs &a, const int32_t *pos, int world, int cap, const float *y, float *out,
                                     bool wbd, cudaStream_t s);
 

@@ -97,6 +97,32 @@ class CudaEPOps:
                                                    _stream_ptr(x.device)), "latent_ep_pack_fixed")
         return rows, meta
 
+    def pack_fixed_merged(self, p: Packed, world: int, cap: int) -> torch.Tensor:
+        """The fixed-capacity blocks with rows and (id, weight) metadata in one byte buffer [world, block]."""
+        x, ids, weights, wbd = p.state
+        d = self._desc(x, ids, weights, wbd)
+        d.send_x, d.send_expert, d.send_weight = p.send_x.data_ptr(), p.send_expert.data_ptr(), p.send_weight.data_ptr()
+        need = C.c_size_t()
+        lib, stream = _lib.lib(), _stream_ptr(x.device)
+        _lib.check(lib.latent_ep_pack_fixed_merged(C.byref(d), world, cap, None, 0, C.byref(need), stream), "size")
+        buf = torch.empty((world, need.value // world), dtype=torch.uint8, device=x.device)
+        _lib.check(lib.latent_ep_pack_fixed_merged(C.byref(d), world, cap, buf.data_ptr(), buf.numel(), None,
+                                                   stream), "latent_ep_pack_fixed_merged")
+        return buf
+
+    def unpack_fixed(self, buf: torch.Tensor, world: int, cap: int, x_dtype, base: int, wbd: bool):
+        """Received merged blocks -> (x rows [world*cap, d], local ids [world*cap, 1], weights [world*cap, 1])."""
+        dev = buf.device
+        d = self.local.n_embd
+        x_out = torch.empty((world * cap, d), dtype=x_dtype, device=dev)
+        ids = torch.empty((world * cap, 1), dtype=torch.int32, device=dev)
+        w = torch.empty((world * cap, 1), dtype=torch.float32, device=dev)
+        _lib.check(_lib.lib().latent_ep_unpack_fixed(
+            buf.data_ptr(), world, cap, d, _X_TYPES[x_dtype], base, self.local.n_expert,
+            _lib.FLAG_WEIGHT_BEFORE_DOWN if wbd else 0, x_out.data_ptr(), ids.data_ptr(), w.data_ptr(), None,
+            _stream_ptr(dev)), "latent_ep_unpack_fixed")
+        return x_out, ids, w
+
     def combine_fixed(self, p: Packed, y_rows: torch.Tensor, world: int, cap: int) -> torch.Tensor:
         x, ids, weights, wbd = p.state
         out = torch.empty((ids.shape[0], x.shape[1]), dtype=torch.float32, device=x.device)
@@ -221,6 +247,18 @@ class ExpertParallelFFN:
         p = self.ops.dispatch(x, ids, weights, wbd)
         send_counts = p.expert_counts.view(G, self.e_local).sum(dim=1).to(torch.int64)
         fused = hasattr(self.ops, "pack_fixed")
+        if hasattr(self.ops, "pack_fixed_merged"):
+            # rows and their (id, weight) metadata in one all-to-all
+            send = self.ops.pack_fixed_merged(p, G, cap)
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send, group=self.group)
+            recv_x, local_ids, rw = self.ops.unpack_fixed(recv, G, cap, x.dtype, self.base, wbd)
+            y = self.ops.local_ffn(recv_x, local_ids, rw, wbd)
+            y_pad = torch.empty((G * cap, d), dtype=torch.float32, device=dev)
+            dist.all_to_all_single(y_pad, y.contiguous(), group=self.group)
+            self._counts = (send_counts, (local_ids.view(G, cap) >= 0).sum(dim=1))
+            self._last = p
+            return self.ops.combine_fixed(p, y_pad, G, cap)
         if fused:
             send_x, send_meta = self.ops.pack_fixed(p, G, cap)
         else:

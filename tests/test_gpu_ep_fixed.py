@@ -81,3 +81,36 @@ def test_pack_fixed_overflow_keeps_the_first_rows_and_is_reported(cuda):
     ok = ops.dispatch(x, torch.stack([ids[:, 0], ids[:, 0] + 1], dim=1).contiguous(), w, False)
     ops.pack_fixed(ok, world, cap)
     ops.check(ok)
+
+
+@pytest.mark.parametrize("wbd", [False, True])
+def test_merged_blocks_carry_the_same_rows_and_metadata(cuda, wbd):
+    """latent_ep_pack_fixed_merged + latent_ep_unpack_fixed (rows and metadata in
+    one buffer, one all-to-all) against the separate blocks of
+    latent_ep_pack_fixed, with the exchange done by hand for 4 ranks: the
+    receiving rank r gets block r of every sender (here one sender)."""
+    dev = torch.device("cuda", 0)
+    cfg = synth.CONFIGS[0]
+    E, world = cfg.n_expert, 4
+    el = E // world
+    es = ExpertSet(synth.make_expert_factors(cfg, dev, experts=range(el)), device=dev, rank=cfg.rank)
+    x, ids, w = synth.make_batch(cfg, dev, n_tokens=40)
+    ids[0, 1] = -1
+    T, k = ids.shape
+    cap = T * min(k, el)
+    ops = CudaEPOps(es, E)
+    p = ops.dispatch(x, ids, w, wbd)
+    rows, meta = ops.pack_fixed(p, world, cap)
+    buf = ops.pack_fixed_merged(p, world, cap)
+    assert buf.shape[0] == world
+    for r in range(world):           # rank r receives block r of this sender: as if world senders sent alike
+        recv = buf[r:r + 1].expand(world, -1).contiguous()
+        rx, lids, rw = ops.unpack_fixed(recv, world, cap, x.dtype, r * el, wbd)
+        blk_meta = meta[r * cap:(r + 1) * cap]
+        live = blk_meta[:, 0] >= 0
+        for g in range(world):
+            sl = slice(g * cap, (g + 1) * cap)
+            assert torch.equal(lids[sl, 0], torch.where(live, blk_meta[:, 0] - r * el, -1)), (r, g)
+            assert torch.equal(rx[sl][live], rows[r * cap:(r + 1) * cap][live]), (r, g)
+            want_w = blk_meta[:, 1].view(torch.float32) if wbd else torch.ones(cap, device=dev)
+            assert torch.equal(rw[sl, 0][live], want_w[live]), (r, g)
