@@ -39,55 +39,63 @@ constexpr int kBK = 64;   // K per stage (128 bytes of f16: one swizzle atom)
 
 // ---------------------------------------------------------------------------
 // Dequantize-transpose: NF4/INT8 factor [K rows][N cols] of every expert into
-// f16 [N][K] rows at dst + e*dst_expert_stride + (row_off + n)*K.
+// f16 [N][K] rows at dst + e*dst_expert_stride + (row_off + n)*K.  One block
+// per (expert, 256-column tile, 64-row block).  Decode: thread t takes row
+// k0 + t % 64 of group column t / 64 (and +4), so that a warp writes 32
+// consecutive k of one n into the [n][k] shared tile (conflict-free); the
+// group loads are L1-cached 16-byte loads.  Store: 8 lanes per output row,
+// each a 16-byte run: every warp store writes four whole 128-byte lines.
+constexpr int kDqK = 64;             // K rows per block
+constexpr int kDqLd = kDqK + 8;      // tile row pitch in halves (144 B)
+
 __global__ void __launch_bounds__(256) k_pf_dequant_t(latent_qmatrix m, __half *dst, int64_t dst_expert_stride,
                                                        int row_off) {
-    __shared__ float tile[64][65];
+    __shared__ __align__(16) __half tile[256][kDqLd];
     __shared__ float lut[16];  // per-thread table indices: shared memory, not the constant cache
     if (threadIdx.x < 16) lut[threadIdx.x] = kNF4Levels[threadIdx.x];
-    __syncthreads();
     const int e = blockIdx.z;
     const QView M = expert_view(m, e);
     const int K = M.rows, N = M.cols;
-    const int k0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-    {
-        const int kk = threadIdx.x >> 2, nn = (threadIdx.x & 3) * 16;
-        const int k = k0 + kk, n = n0 + nn;
-        if (k < K && n < N) {
-            const int64_t g = tile_group(K, N, k, n);
-            const uint2 q = __ldg(reinterpret_cast<const uint2 *>(M.codes + g * 16 + ((n & 31) >> 1)));
-            const uint16_t sb = __ldg(M.scales + g);
-            const float sc = half_bits_to_float(sb & 0x7FFFu);
-            uint32_t idx;
-            if ((sb & 0x8000u) && M.i8.present() && M.i8.is_int8(g, &idx)) {
-                const uint2 hi = __ldg(reinterpret_cast<const uint2 *>(M.i8.hi + (int64_t)idx * 16 + ((n >> 4) & 1) * 8));
+    const int c = blockIdx.x;
+    const int ng = min(8, (N >> 5) - 8 * c);
+    const int k0 = blockIdx.y * kDqK;
+    const int nk = min(kDqK, K - k0);
+    const int64_t q0 = (int64_t)c * K * 8 + (int64_t)k0 * ng;  // tile_group(K, N, k0, 256 c)
+    __syncthreads();
+    const int kk = threadIdx.x % kDqK;
+    for (int gi = threadIdx.x / kDqK; gi < ng; gi += 256 / kDqK) {
+        if (kk >= nk) continue;
+        const int64_t g = q0 + (int64_t)kk * ng + gi;
+        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(M.codes) + g);
+        const uint16_t sb = __ldg(M.scales + g);
+        const float sc = half_bits_to_float(sb & 0x7FFFu);
+        uint4 h = make_uint4(0u, 0u, 0u, 0u);
+        uint32_t idx;
+        const bool i8 = (sb & 0x8000u) && M.i8.present() && M.i8.is_int8(g, &idx);
+        if (i8) h = __ldg(reinterpret_cast<const uint4 *>(M.i8.hi + (int64_t)idx * 16));
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w}, hw[4] = {h.x, h.y, h.z, h.w};
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    tile[kk][nn + j] = __fmul_rn(int8_elem(q.x, hi.x, j), sc);
-                    tile[kk][nn + 8 + j] = __fmul_rn(int8_elem(q.y, hi.y, j), sc);
-                }
-            } else {
+        for (int s = 0; s < 4; ++s) {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    tile[kk][nn + j] = __fmul_rn(lut[(q.x >> (4 * j)) & 15u], sc);
-                    tile[kk][nn + 8 + j] = __fmul_rn(lut[(q.y >> (4 * j)) & 15u], sc);
-                }
+            for (int j = 0; j < 8; ++j) {
+                const float v = i8 ? int8_elem(w[s], hw[s], j) : lut[(w[s] >> (4 * j)) & 15u];
+                tile[gi * 32 + s * 8 + j][kk] = __float2half_rn(__fmul_rn(v, sc));
             }
         }
     }
     __syncthreads();
-    const int nn = threadIdx.x >> 2, kk = (threadIdx.x & 3) * 16;
-    const int n = n0 + nn, k = k0 + kk;
-    if (n < N && k < K) {
-        __half *out = dst + (int64_t)e * dst_expert_stride + (int64_t)(row_off + n) * K + k;
-        if (k + 16 <= K) {
-            __align__(16) __half h[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) h[j] = __float2half_rn(tile[kk + j][nn]);
-            reinterpret_cast<uint4 *>(out)[0] = reinterpret_cast<uint4 *>(h)[0];
-            reinterpret_cast<uint4 *>(out)[1] = reinterpret_cast<uint4 *>(h)[1];
+    const int nn = ng * 32;
+    for (int i = threadIdx.x; i < nn * (kDqK / 8); i += blockDim.x) {
+        const int n = i >> 3, ch = i & 7;
+        const int kc = ch * 8;
+        if (kc >= nk) continue;
+        __half *out = dst + (int64_t)e * dst_expert_stride + (int64_t)(row_off + 256 * c + n) * K + k0 + kc;
+        const uint4 v = *reinterpret_cast<const uint4 *>(&tile[n][kc]);
+        if (kc + 8 <= nk) {
+            *reinterpret_cast<uint4 *>(out) = v;
         } else {
-            for (int j = 0; j < 16 && k + j < K; ++j) out[j] = __float2half_rn(tile[kk + j][nn]);
+            const __half *hv = reinterpret_cast<const __half *>(&v);
+            for (int j = 0; kc + j < nk; ++j) out[j] = hv[j];
         }
     }
 }
@@ -461,7 +469,7 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, ui
 }
 
 cudaError_t launch_dequant_t(const latent_qmatrix &m, int E, __half *dst, int64_t stride, int row_off, cudaStream_t s) {
-    dim3 grid((unsigned)((m.cols + 63) / 64), (unsigned)((m.rows + 63) / 64), (unsigned)E);
+    dim3 grid((unsigned)((m.cols + 255) / 256), (unsigned)((m.rows + kDqK - 1) / kDqK), (unsigned)E);
     k_pf_dequant_t<<<grid, 256, 0, s>>>(m, dst, stride, row_off);
     return cudaGetLastError();
 }
