@@ -49,8 +49,8 @@
 // pairs, selected by the sign bit of the group's scale (the INT8 flag).  An
 // INT8 group adds the high nibbles afterwards: int8 = lo + 16 * sext(hi);
 // the warp's INT8 rows are listed in shared memory and spread over its lanes,
-// which decode them arithmetically (sext(n) = float(0x4B000000 | (n ^ 8)) -
-// (2^23 + 8)).
+// which look the high nibbles up in the unsigned table at byte ^ 0x88 and
+// subtract 8 (sext(n) = (n ^ 8) - 8).
 //
 // Every wait is bounded (kWaitNs): a wait that gives up sets kErrTimeout,
 // which every other wait sees, and the kernel unwinds (the producer lets its
@@ -913,13 +913,14 @@ __device__ __forceinline__ void consume_stage(const Args &a, const Hdr &h, uint3
             xs[4 * t4 + 2] = pack2(xv[t4].z * sc16, xv[t4].z * sc16);
             xs[4 * t4 + 3] = pack2(xv[t4].w * sc16, xv[t4].w * sc16);
         }
-        const u64 bias = pack2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
+        // sext(n) = (n ^ 8) - 8: table 1 (unsigned nibble pairs) at byte ^ 0x88, minus 8
+        const u64 bias = pack2(-8.f, -8.f);
+        const uint32_t lr1 = wc.lb | 0x80u;
+        const uint32_t hx[2] = {hw[0] ^ 0x88888888u, hw[1] ^ 0x88888888u};
 #pragma unroll
         for (int b = 0; b < C::NB; ++b) {
-            const uint32_t byte = (hw[b >> 2] >> (8 * (b & 3))) & 0xFFu;
-            const float lo = __uint_as_float(((byte & 0xFu) ^ 0x8u) | 0x4B000000u);
-            const float hi = __uint_as_float(((byte >> 4) ^ 0x8u) | 0x4B000000u);
-            const u64 vv = fadd2(pack2(lo, hi), bias);
+            const uint32_t addr = __byte_perm(hx[b >> 2], lr1, 0x7604u | ((uint32_t)(b & 3) << 4));
+            const u64 vv = fadd2(lds64(addr), bias);
 #pragma unroll
             for (int t = 0; t < NT; ++t) ffma2(acc[t * C::NB + b], xs[t], vv);
         }
