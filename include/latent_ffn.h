@@ -39,8 +39,23 @@
  *   i8_hi   uint8  [n_int8_groups][16]        high nibbles of the INT8
  *                                              groups in (expert, q) order,
  *                                              same nibble order as codes
- * i8_mask/i8_base/i8_hi are NULL when no group is INT8; otherwise all three
- * start on a 16-byte boundary (codes and scales too).  The tile order lets
+ *   i8_blocks int32 [n_blocks][12]           per block b = (e*tiles + c)*row_blocks
+ *                                              + s (expert e, 256-column tile c,
+ *                                              128-row block s; tiles = ceil(cols/256),
+ *                                              row_blocks = ceil(rows/128)): words
+ *                                              0..8 cumulative entry offsets of
+ *                                              the block's group columns 0..7
+ *                                              (word 0 = 0, word 8 = the block's
+ *                                              INT8 groups), word 9 the block's
+ *                                              first entry in i8_list (a multiple
+ *                                              of 4), word 10 its first record in
+ *                                              i8_hi, word 11 zero
+ *   i8_list uint32 [..]                       one entry per INT8 group:
+ *                                              (row in block << 16) | (record -
+ *                                              word 10), by column then row; each
+ *                                              block's run padded to 4 entries
+ * i8_mask/i8_base/i8_hi/i8_blocks/i8_list are NULL when no group is INT8;
+ * otherwise all five start on a 16-byte boundary (codes and scales too).  The tile order lets
  * a kernel streaming a row range of one column tile read its codes, scales
  * and INT8 records as three contiguous runs (latent_b200/format.py packs it).
  * cols must be a multiple of 32; the rank dimension may be zero-padded
@@ -65,7 +80,7 @@ struct CUevent_st;  /* cudaEvent_t */
 #define LATENT_API
 #endif
 
-#define LATENT_ABI_VERSION 3
+#define LATENT_ABI_VERSION 4
 
 typedef enum latent_status {
     LATENT_OK = 0,
@@ -113,6 +128,8 @@ typedef struct latent_qmatrix {
     const uint32_t *i8_mask;
     const uint32_t *i8_base;
     const uint8_t *i8_hi;
+    const int32_t *i8_blocks;
+    const uint32_t *i8_list;
     int64_t rows;
     int64_t cols;
 } latent_qmatrix;

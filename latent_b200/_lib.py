@@ -39,6 +39,8 @@ class QMatrix(C.Structure):
         ("i8_mask", C.c_void_p),
         ("i8_base", C.c_void_p),
         ("i8_hi", C.c_void_p),
+        ("i8_blocks", C.c_void_p),
+        ("i8_list", C.c_void_p),
         ("rows", C.c_int64),
         ("cols", C.c_int64),
     ]
@@ -206,7 +208,7 @@ def lib() -> C.CDLL:
                 fn = getattr(h, name)
                 fn.restype = res
                 fn.argtypes = args
-            if h.latent_abi_version() != 3:
+            if h.latent_abi_version() != 4:
                 raise RuntimeError("liblatent_b200.so ABI version mismatch")
             _lib = h
     return _lib

@@ -41,9 +41,10 @@ int check_qmatrix(const latent_qmatrix &m, int64_t rows, int64_t cols, bool need
     if (!need_ptrs) return LATENT_OK;
     if (!m.codes || !m.scales) return LATENT_ERR_INVALID;
     if (!aligned(m.codes, 16) || !aligned(m.scales, 16)) return LATENT_ERR_ALIGN;
-    const bool any = m.i8_mask || m.i8_base || m.i8_hi;
-    if (any && !(m.i8_mask && m.i8_base && m.i8_hi)) return LATENT_ERR_INVALID;
-    if (m.i8_hi && (!aligned(m.i8_hi, 16) || !aligned(m.i8_mask, 16) || !aligned(m.i8_base, 16)))
+    const bool any = m.i8_mask || m.i8_base || m.i8_hi || m.i8_blocks || m.i8_list;
+    if (any && !(m.i8_mask && m.i8_base && m.i8_hi && m.i8_blocks && m.i8_list)) return LATENT_ERR_INVALID;
+    if (m.i8_hi && (!aligned(m.i8_hi, 16) || !aligned(m.i8_mask, 16) || !aligned(m.i8_base, 16) ||
+                    !aligned(m.i8_blocks, 16) || !aligned(m.i8_list, 16)))
         return LATENT_ERR_ALIGN;
     return LATENT_OK;
 }

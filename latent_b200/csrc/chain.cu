@@ -27,7 +27,7 @@
 //    entry and INT8 record boundaries while it issues earlier items, and
 //    fills a ring of kSlots stages (128 rows of one tile) with cp.async.bulk
 //    copies completing on the slot's mbarrier: codes, scales, INT8 records
-//    (and mask/base words by cp.async).  Weight copies never wait for a
+//    and the stage's INT8 list block.  Weight copies never wait for a
 //    dependency.
 //  - the input warp follows the stage headers: P1 stages get their x rows
 //    gathered, converted and transposed into the slot; later phases wait for
@@ -74,8 +74,8 @@ constexpr int kNW = 8;                     // consumer warps
 constexpr int kThreads = (kNW + 2) * 32;   // + the producer and the input warp
 constexpr int kSlots = 4;
 constexpr int kStageRows = 128;
+constexpr int kListCap = 384;              // INT8 list entries staged per stage (more are read from global memory)
 constexpr int kRecCap = 384;               // INT8 records staged per stage (more are read from global memory)
-constexpr int kWordCap = 48;               // INT8 mask (and base) words staged per stage
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
 // Slot layout (bytes from the slot base, which is 1024-byte aligned: full
@@ -83,24 +83,23 @@ constexpr unsigned long long kWaitNs = 2000000000ull;
 constexpr int kOffCodes = 0;
 constexpr int kOffScales = kOffCodes + kStageRows * 128;
 constexpr int kOffIn = kOffScales + kStageRows * 16;
-constexpr int kOffMask = kOffIn + kStageRows * 8 * 4;
-constexpr int kOffBase = kOffMask + kWordCap * 4;
-constexpr int kOffRec = kOffBase + kWordCap * 4;
+constexpr int kOffLoff = kOffIn + kStageRows * 8 * 4;  // the stage's INT8 list block words (12 x int32)
+constexpr int kOffList = kOffLoff + 64;                // its INT8 list entries (kListCap)
+constexpr int kOffRec = kOffList + kListCap * 4;
 constexpr int kOffHdr = kOffRec + kRecCap * 16;
 constexpr int kSlotBytes = (kOffHdr + 128 + 1023) / 1024 * 1024;
 static_assert(kOffHdr % 16 == 0, "slot alignment");
 
-// Dynamic shared memory: region A (barriers, INT8 row lists, cross-warp
+// Dynamic shared memory: region A (barriers, per-warp item data, cross-warp
 // buffer, slot 0) below shared address 64 K, the lookup table at
 // [64 K, 128 K), slots 1.. above it.
 constexpr int kBarBytes = 256;                        // mbarriers: full, empty, hdr per slot; consumers
 static_assert(8 * (3 * kSlots + 1) <= kBarBytes, "mbarrier area");
-constexpr int kListBytes = kNW * kStageRows * 4;      // per-warp INT8 row lists
 constexpr int kPreBytes = kNW * 64;                   // per-warp slots and router weights of the current item
 constexpr int kXbufBytes = 2 * kNW * 32 * 8 * 4;      // [matrix][warp][lane][8] cross-warp partial sums
 constexpr uint32_t kTableAddr = 65536;
 constexpr int kTableBytes = 65536;
-constexpr int kRegionA = kBarBytes + kListBytes + kPreBytes + kXbufBytes + 1024 + kSlotBytes;  // + slot 0 alignment
+constexpr int kRegionA = kBarBytes + kPreBytes + kXbufBytes + 1024 + kSlotBytes;  // + slot 0 alignment
 constexpr int kMaxSmemBase = 65536 - kRegionA;  // dynamic shared memory must start below this
 constexpr int kDynEnd = (int)kTableAddr + kTableBytes + (kSlots - 1) * kSlotBytes;
 static_assert(kMaxSmemBase > 4096, "region A");
@@ -116,8 +115,8 @@ struct Hdr {
     int tc, tile_w, ng, nrows;
     int row0, nt, NT, off;
     int first_pos, flags, rec0, nrec_s;  // first INT8 record, records staged in the slot
-    int ws, q0, nrec, in_row;            // first staged mask word (absolute), first group (expert-local),
-                                         // INT8 records of the stage, first input row
+    int list0, q0, nrec, in_row;         // first INT8 list entry of the stage's block, first group
+                                         // (expert-local), INT8 records of the stage, first input row
 };
 static_assert(sizeof(Hdr) <= 128, "header");
 
@@ -241,15 +240,6 @@ __device__ __forceinline__ void bulk_g2s_plain(uint32_t dst, const void *src, ui
                  "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
 }
-// 16-byte cp.async that reads `src_bytes` (0..16) and zero-fills the rest.
-__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void *src, uint32_t src_bytes) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-// Makes the slot's barrier wait for this thread's cp.async copies.
-__device__ __forceinline__ void cp_async_bar_arrive(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-
 // --- shared-memory loads and packed fp32 ---------------------------------------
 __device__ __forceinline__ u64 pack2(float a, float b) {
     u64 r;
@@ -299,9 +289,6 @@ __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
 }
 __device__ __forceinline__ void sts_v4(uint32_t addr, int x, int y, int z, int w) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
-}
-__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
-    asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 __device__ __forceinline__ void sts_f4(uint32_t addr, float4 v) {
     asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
@@ -417,63 +404,27 @@ __device__ __forceinline__ const float *input_base(const Args &a, int p, int off
     return a.sb + (int64_t)off * a.r;
 }
 
-// INT8 records before expert-local group q of expert e are
-// base[w] + popc(mask[w] & low) (records in (expert, group) order; base words
-// count over all experts): the word and the low-bit mask.
-__device__ __forceinline__ void int8_word(const latent_qmatrix &m, int e, int64_t q, int64_t &wi, uint32_t &low) {
-    const int64_t groups = m.rows * m.cols / 32, words = (groups + 31) / 32;
-    int64_t w = q >> 5;
-    if (w >= words) {  // q == groups on a word boundary: all bits of the last word count
-        w = words - 1;
-        low = 0xFFFFFFFFu;
-    } else {
-        low = (q & 31) ? ((1u << (q & 31)) - 1u) : 0u;
-    }
-    wi = (int64_t)e * words + w;
-}
-
-// Raw INT8 boundary words of stage `lane` of an item (mask/base at its first
-// and end group), loaded one item before they are used.
+// INT8 list block of stage `lane` of an item (128-row block of one column
+// tile of one expert, see latent_qmatrix.i8_blocks): its entry count, first
+// list entry and first record, loaded one item before they are used.
 struct MetaRaw {
-    uint32_t m0, b0, m1, b1;
+    int n, list0, rec0, b;
 };
 
 __device__ MetaRaw meta_load(const Args &a, const Item &it, int lane) {
-    MetaRaw r{0u, 0u, 0u, 0u};
+    MetaRaw r{0, 0, 0, -1};
     if (lane >= it.n_stages) return r;
     int m, row0, n;
     stage_rows(it, lane, m, row0, n);
     const latent_qmatrix &qm = phase_mat(a, it.phase, m);
-    if (!qm.i8_mask) return r;
-    const int ng = it.tile_w >> 5;
-    const int64_t q0 = (int64_t)it.tc * qm.rows * 8 + (int64_t)row0 * ng;
-    int64_t w0, w1;
-    uint32_t l0, l1;
-    int8_word(qm, it.ve.x, q0, w0, l0);
-    int8_word(qm, it.ve.x, q0 + (int64_t)n * ng, w1, l1);
-    r.m0 = __ldg(qm.i8_mask + w0);
-    r.b0 = __ldg(qm.i8_base + w0);
-    r.m1 = __ldg(qm.i8_mask + w1);
-    r.b1 = __ldg(qm.i8_base + w1);
+    if (!qm.i8_blocks) return r;
+    const int tiles = (int)((qm.cols + 255) >> 8), rblk = (int)((qm.rows + kStageRows - 1) / kStageRows);
+    r.b = (it.ve.x * tiles + it.tc) * rblk + row0 / kStageRows;
+    const int4 w2 = __ldg(reinterpret_cast<const int4 *>(qm.i8_blocks + (int64_t)r.b * 12 + 8));  // words 8..11
+    r.n = w2.x;
+    r.list0 = w2.y;
+    r.rec0 = w2.z;
     return r;
-}
-
-// Records before stage s's first group and before its end group.
-__device__ __forceinline__ void stage_records(const Args &a, const Item &it, int s, const MetaRaw &mr, uint32_t &rec0,
-                                              uint32_t &rec1) {
-    rec0 = rec1 = 0;
-    int m, row0, n;
-    stage_rows(it, s, m, row0, n);
-    const latent_qmatrix &qm = phase_mat(a, it.phase, m);
-    if (!qm.i8_mask) return;
-    const int ng = it.tile_w >> 5;
-    const int64_t q0 = (int64_t)it.tc * qm.rows * 8 + (int64_t)row0 * ng;
-    int64_t w0, w1;
-    uint32_t l0, l1;
-    int8_word(qm, it.ve.x, q0, w0, l0);
-    int8_word(qm, it.ve.x, q0 + (int64_t)n * ng, w1, l1);
-    rec0 = mr.b0 + __popc(mr.m0 & l0);
-    rec1 = mr.b1 + __popc(mr.m1 & l1);
 }
 
 // --- producer --------------------------------------------------------------------
@@ -489,11 +440,11 @@ __device__ __forceinline__ int mat_index(int phase, int m) { return phase == 1 ?
 struct MatView {
     const uint8_t *codes;    // the expert's codes
     const uint16_t *scales;  // the expert's scales
-    const uint32_t *mask, *base;
+    const int32_t *blocks;   // INT8 list blocks and entries (latent_qmatrix.i8_blocks / i8_list)
+    const uint32_t *list;
     const uint8_t *hi;
     int64_t rows;
     int64_t cbyte;           // byte offset of the expert's codes in the stacked tensor
-    int64_t wbase, wend;     // the expert's first mask word, end of its words
 };
 
 __device__ __forceinline__ MatView mat_view(const Args &a, int phase, int m, int e) {
@@ -503,13 +454,10 @@ __device__ __forceinline__ MatView mat_view(const Args &a, int phase, int m, int
     v.cbyte = (int64_t)e * (epe >> 1);
     v.codes = qm.codes + v.cbyte;
     v.scales = qm.scales + (int64_t)e * (epe >> 5);
-    v.mask = qm.i8_mask;
-    v.base = qm.i8_base;
+    v.blocks = qm.i8_blocks;
+    v.list = qm.i8_list;
     v.hi = qm.i8_hi;
     v.rows = qm.rows;
-    const int64_t words = ((epe >> 5) + 31) >> 5;
-    v.wbase = (int64_t)e * words;
-    v.wend = v.wbase + words;
     return v;
 }
 
@@ -559,9 +507,7 @@ __device__ void producer_run(const Args &a, const CodeMaps &maps, const Geo &g, 
         const int4 ve = cur.ve;
         const int NT = ve.z <= 4 ? 4 : 8;
         const int ng = cur.tile_w >> 5;
-        // this lane's stage (s = lane): its INT8 record range, from the boundary words
-        uint32_t my_rec0 = 0, my_rec1 = 0;
-        if (lane < cur.n_stages) stage_records(a, cur, lane, mc, my_rec0, my_rec1);
+        // this lane's stage (s = lane): its INT8 list block
         // the item's matrices in registers (P2 covers gate and up)
         const MatView mv0 = mat_view(a, ph, cur.m0, ve.x);
         const MatView mv1 = ph == 2 ? mat_view(a, ph, 1, ve.x) : mv0;
@@ -579,15 +525,15 @@ __device__ void producer_run(const Args &a, const CodeMaps &maps, const Geo &g, 
             MatView mv;
             mv.codes = second ? mv1.codes : mv0.codes;
             mv.scales = second ? mv1.scales : mv0.scales;
-            mv.mask = second ? mv1.mask : mv0.mask;
-            mv.base = second ? mv1.base : mv0.base;
+            mv.blocks = second ? mv1.blocks : mv0.blocks;
+            mv.list = second ? mv1.list : mv0.list;
             mv.hi = second ? mv1.hi : mv0.hi;
             mv.rows = second ? mv1.rows : mv0.rows;
             mv.cbyte = second ? mv1.cbyte : mv0.cbyte;
-            mv.wbase = second ? mv1.wbase : mv0.wbase;
-            mv.wend = second ? mv1.wend : mv0.wend;
-            const uint32_t rec0 = __shfl_sync(0xffffffffu, my_rec0, s & 31);
-            const uint32_t nrec = __shfl_sync(0xffffffffu, my_rec1, s & 31) - rec0;
+            const uint32_t rec0 = (uint32_t)__shfl_sync(0xffffffffu, mc.rec0, s & 31);
+            const uint32_t nrec = (uint32_t)__shfl_sync(0xffffffffu, mc.n, s & 31);
+            const int list0 = __shfl_sync(0xffffffffu, mc.list0, s & 31);
+            const int blk = __shfl_sync(0xffffffffu, mc.b, s & 31);
             const uint32_t nrec_s = min(nrec, (uint32_t)kRecCap);
             const int64_t q0 = (int64_t)cur.tc * mv.rows * 8 + (int64_t)row0 * ng;
             int fl = 0;
@@ -597,42 +543,30 @@ __device__ void producer_run(const Args &a, const CodeMaps &maps, const Geo &g, 
             const int mi = mat_index(ph, m);
             const bool swz = ng == 8 && n == kStageRows && ((tma_bits >> mi) & 1u);
             if (swz) fl |= kSwz;
-            int ws = 0;
-            if (mv.mask) {  // the stage's mask/base words, whole 16-byte chunks; lanes 0-15 mask, 16-31 base
-                const int64_t wfirst = mv.wbase + (q0 >> 5);
-                const int64_t wlast = mv.wbase + ((q0 + (int64_t)n * ng - 1) >> 5);
-                const int64_t wlo = wfirst & ~(int64_t)3;
-                ws = (int)wlo;
-                const int chunks = (int)((((wlast + 4) & ~(int64_t)3) - wlo) >> 2);
-                const int ck = lane & 15;
-                if (ck < chunks) {
-                    const int64_t w0 = wlo + 4 * ck;
-                    const int64_t avail = mv.wend - w0;  // words past the arrays' end are zero-filled, not read
-                    const uint32_t src_bytes = avail >= 4 ? 16u : avail > 0 ? (uint32_t)(avail * 4) : 0u;
-                    const uint32_t *srcp = (lane < 16 ? mv.mask : mv.base) + (src_bytes ? w0 : 0);
-                    cp_async16_zfill(sbase + (lane < 16 ? kOffMask : kOffBase) + 16 * ck, srcp, src_bytes);
-                }
-                cp_async_bar_arrive(full);
-            }
-            __syncwarp();  // the cp.async arrivals are registered before the slot can complete
             if (lane == 0) {
                 const uint32_t hp = sbase + kOffHdr;
                 sts_v4(hp, ph, cur.v, ve.x, m);
                 sts_v4(hp + 16, cur.tc, cur.tile_w, ng, n);
                 sts_v4(hp + 32, row0, ve.z, NT, ve.w);
                 sts_v4(hp + 48, ve.y, fl, (int)rec0, (int)nrec_s);
-                sts_v4(hp + 64, ws, (int)q0, (int)nrec, (ph == 2 ? m * r_rows : 0) + row0);
+                sts_v4(hp + 64, list0, (int)q0, (int)nrec, (ph == 2 ? m * r_rows : 0) + row0);
                 const uint32_t cbytes = (uint32_t)n * ng * 16, sbytes = (uint32_t)n * ng * 2;
                 const uint32_t ibytes = ph >= 2 ? (uint32_t)n * NT * 4 : 0u;  // P1 inputs are stored by the input warp
-                const uint32_t rbytes = mv.mask ? nrec_s * 16 : 0u;
+                const uint32_t rbytes = nrec_s * 16;
+                // the block's list words and its first entries (blocks pad their entries to 4: 16-byte copies)
+                const uint32_t lbytes = nrec ? 48u + min((nrec + 3u) & ~3u, (uint32_t)kListCap) * 4u : 0u;
                 // the input copy (issued by the input warp) completes on the same phase
-                mbar_arrive_tx(full, cbytes + sbytes + ibytes + rbytes);
+                mbar_arrive_tx(full, cbytes + sbytes + ibytes + rbytes + lbytes);
                 if (swz)  // rows of 128 bytes: row index of the stage's first code byte
                     tma_load_2d(sbase + kOffCodes, &maps.m[mi], 0, (int)((mv.cbyte + q0 * 16) >> 7), full, policy);
                 else
                     bulk_g2s(sbase + kOffCodes, mv.codes + q0 * 16, cbytes, full, policy);
                 bulk_g2s(sbase + kOffScales, mv.scales + q0, sbytes, full, policy);
                 if (rbytes) bulk_g2s(sbase + kOffRec, mv.hi + (int64_t)rec0 * 16, rbytes, full, policy);
+                if (lbytes) {
+                    bulk_g2s(sbase + kOffLoff, mv.blocks + (int64_t)blk * 12, 48u, full, policy);
+                    bulk_g2s(sbase + kOffList, mv.list + list0, lbytes - 48u, full, policy);
+                }
                 mbar_arrive(hdrb);
             }
             __syncwarp();
@@ -844,35 +778,19 @@ __device__ __forceinline__ void consume_stage(const Args &a, const Hdr &h, uint3
             for (int t = 0; t < NT; ++t) ffma2(acc[t * C::NB + b], xs[t], vv);
         }
     }
-    // INT8 groups: add 16 * sext(hi) for the warp's INT8 rows of group g.
-    // Lane j flags rows rr0 + 32q + j; the flagged rows go to the warp's list
-    // in shared memory, whose entries the row slots then take in turn.
+    // INT8 groups: add 16 * sext(hi) for the warp's INT8 rows of group g.  The
+    // stage's list block holds column g's entries (row, record) in row order;
+    // the row slots take them in turn.
+    if (h.nrec == 0) return;
     const latent_qmatrix &qm = phase_mat(a, h.kind, h.m);
-    if (!qm.i8_mask) return;
-    const int words = (int)((qm.rows * qm.cols / 32 + 31) / 32);
-    const int wrel = h.e * words - h.ws;  // staged word of expert-local word w: w + wrel
-    int tot = 0;
-#pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {
-        const int r = rr0 + 32 * q4 + lane;
-        const bool f = r < rr1 && (lds16(scales + r * srow) & 0x8000u) != 0;
-        const uint32_t m = __ballot_sync(0xffffffffu, f);
-        if (f) {  // record index of (row r, group g), relative to the stage's first record
-            const int qg = h.q0 + r * h.ng + g;
-            const int widx = (qg >> 5) + wrel;
-            const uint32_t mw = lds32(sb + kOffMask + 4 * widx), bw = lds32(sb + kOffBase + 4 * widx);
-            const uint32_t ri = bw + __popc(mw & ((1u << (qg & 31)) - 1u)) - (uint32_t)h.rec0;
-            sts32(wc.list + 4 * (tot + __popc(m & ((1u << lane) - 1u))), (ri << 8) | (uint32_t)(r - rr0));
-        }
-        tot += __popc(m);
-    }
-    if (tot == 0) return;
-    __syncwarp();
+    const int o0 = (int)lds32(sb + kOffLoff + 4 * g);
+    const int o1 = min((int)lds32(sb + kOffLoff + 4 * (g + 1)), h.nrec);  // tables are not trusted past nrec
 #pragma unroll 1
-    for (int k = rs; k < tot; k += C::S) {
-        const uint32_t ent = lds32(wc.list + 4 * k);
-        const int r = rr0 + (int)(ent & 0xFFu);
-        const uint32_t ri = ent >> 8;
+    for (int k = o0 + rs; k < o1; k += C::S) {
+        const uint32_t ent = k < kListCap ? lds32(sb + kOffList + 4 * k) : __ldg(qm.i8_list + h.list0 + k);
+        const int r = (int)(ent >> 16);
+        if (r < rr0 || r >= rr1) continue;  // another warp's rows
+        const uint32_t ri = ent & 0xFFFFu;
         const uint32_t sbits = lds16(scales + r * srow);
         float4 xv[NT / 4];
 #pragma unroll
@@ -890,7 +808,7 @@ __device__ __forceinline__ void consume_stage(const Args &a, const Hdr &h, uint3
                 hw[1] = 0;
             }
         } else {
-            if (ri >= (uint32_t)h.nrec) {  // a scale flags INT8 where the mask does not: bad tables
+            if (ri >= (uint32_t)h.nrec) {  // an entry past the block's records: bad tables
                 if (ch == 0) atomicOr(a.err, kErrLayout);
                 continue;
             }
@@ -925,7 +843,6 @@ __device__ __forceinline__ void consume_stage(const Args &a, const Hdr &h, uint3
             for (int t = 0; t < NT; ++t) ffma2(acc[t * C::NB + b], xs[t], vv);
         }
     }
-    __syncwarp();  // the list is rewritten by the next stage
 }
 
 // Lane reduce-scatter over the row slots: afterwards lane (rs, ch) holds
@@ -1172,7 +1089,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(Args args, const __grid_c
         return;
     }
     uint8_t *ctl = dsm;
-    uint8_t *xbuf = ctl + kBarBytes + kListBytes + kPreBytes;
+    uint8_t *xbuf = ctl + kBarBytes + kPreBytes;
     Slots slot_ptr;
     {
         const uint32_t s0 = (smem_u32(xbuf + kXbufBytes) + 1023u) & ~1023u;  // 1024-byte aligned
@@ -1238,8 +1155,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_chain(Args args, const __grid_c
         wc.w = warp;
         wc.lane = lane;
         wc.lb = kTableAddr | (uint32_t)((lane & 15) * 8);
-        wc.list = smem_u32(ctl + kBarBytes + warp * kStageRows * 4);
-        wc.pre = reinterpret_cast<int *>(ctl + kBarBytes + kListBytes + warp * 64);
+        wc.pre = reinterpret_cast<int *>(ctl + kBarBytes + warp * 64);
         wc.xbuf = xbuf;
         wc.zeroed = false;
         wc.pend_kind = -1;

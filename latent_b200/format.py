@@ -193,6 +193,60 @@ def tile_order(rows: int, cols: int, device=None) -> torch.Tensor:
     return torch.cat(parts)
 
 
+BLOCK_ROWS = 128   # rows of an INT8 list block (one decode stage)
+BLOCK_WORDS = 12   # int32 words per block in i8_blocks
+
+
+def int8_block_lists(is_i8: torch.Tensor, rows: int, cols: int):
+    """Per-block INT8 group lists of a stacked factor (the decode kernel's staging tables).
+
+    ``is_i8``: bool [E, g] in device (tile-major) group order.  A block is
+    (expert e, 256-column tile c, 128-row block s), index
+    b = (e * tiles + c) * row_blocks + s.  ``i8_blocks`` int32 [n_blocks, 12]:
+    words 0..8 are the cumulative entry offsets of the block's group columns
+    0..7 (column j's entries are [w[j], w[j+1]), w[0] = 0, w[8] = the block's
+    INT8 groups), word 9 the index of the block's first entry in ``i8_list``
+    (a multiple of 4), word 10 the block's first INT8 record in ``i8_hi``.
+    ``i8_list`` uint32 (as int32): one entry per INT8 group, (row in block << 16)
+    | (record index - word 10), sorted by column then row, each block's run
+    padded to a multiple of 4 entries.
+    """
+    dev = is_i8.device
+    E, g = is_i8.shape
+    tiles = (cols + 255) // 256
+    rblk = (rows + BLOCK_ROWS - 1) // BLOCK_ROWS
+    nb = E * tiles * rblk
+    q = torch.arange(g, device=dev)
+    c = torch.div(q, rows * 8, rounding_mode="floor")
+    within = q - c * rows * 8
+    ng = torch.clamp(cols // GROUP - 8 * c, max=8)
+    row = torch.div(within, ng, rounding_mode="floor")
+    gi = within - row * ng
+    blk = c * rblk + torch.div(row, BLOCK_ROWS, rounding_mode="floor")                # per-expert block
+    flag = is_i8.reshape(E, g)
+    e_idx, q_idx = torch.nonzero(flag, as_tuple=True)                                 # (e, q) order = record order
+    rec = torch.arange(e_idx.numel(), device=dev)
+    b = e_idx * (tiles * rblk) + blk[q_idx]
+    counts = torch.bincount(b, minlength=nb)
+    first_rec = torch.cumsum(counts, 0) - counts
+    col_counts = torch.bincount(b * 8 + gi[q_idx], minlength=nb * 8).view(nb, 8)
+    padded = (counts + 3) // 4 * 4
+    blk0 = torch.cumsum(padded, 0) - padded
+    words = torch.zeros((nb, BLOCK_WORDS), dtype=torch.int64, device=dev)
+    words[:, 1:9] = torch.cumsum(col_counts, 1)
+    words[:, 9] = blk0
+    words[:, 10] = first_rec
+    # entries sorted by (block, column, row); rows within a block are BLOCK_ROWS apart at most
+    rib = row[q_idx] % BLOCK_ROWS
+    key = (b * 8 + gi[q_idx]) * BLOCK_ROWS + rib
+    order = torch.argsort(key)
+    b_s = b[order]
+    pos = torch.arange(order.numel(), device=dev) - (torch.cumsum(counts, 0) - counts)[b_s]   # rank in block
+    entries = torch.zeros(int(padded.sum()) if nb else 0, dtype=torch.int64, device=dev)
+    entries[blk0[b_s] + pos] = (rib[order] << 16) | (rec[order] - first_rec[b_s])
+    return words.to(torch.int32).contiguous(), entries.to(torch.int32).contiguous()
+
+
 class StackedFactor:
     """One factor kind of all experts, device-resident, as a ``latent_qmatrix``.
 
@@ -200,8 +254,9 @@ class StackedFactor:
     [E, g, 16], ``scales`` int16 (fp16 bits) [E, g] with g = rows*cols/32,
     and, when any group is INT8, ``i8_mask`` / ``i8_base`` int32 [E, words]
     (bit q of expert e's mask marks an INT8 group; base = INT8 groups before
-    the word over all experts) and ``i8_hi`` uint8 [n_int8, 16] in (expert, q)
-    order.
+    the word over all experts), ``i8_hi`` uint8 [n_int8, 16] in (expert, q)
+    order, and the per-block lists ``i8_blocks`` / ``i8_list`` of
+    ``int8_block_lists`` (the decode kernel stages these instead of the mask).
     """
 
     def __init__(self, factors: Sequence[GroupedFactor], device):
@@ -235,16 +290,20 @@ class StackedFactor:
             self.i8_base = base.to(torch.int32).view(E, words).contiguous()
             hi = torch.stack([f.hi.to(dev).reshape(g, 16) for f in factors])[:, perm].reshape(E * g, 16)
             self.i8_hi = hi[is_i8.reshape(-1)].contiguous()
+            self.i8_blocks, self.i8_list = int8_block_lists(is_i8, rows, cols)
+            n_blk = self.i8_blocks[:, 8].view(E, -1).to(torch.int64)
+            # decode reads a block's 48-byte word row and its padded entries when it has INT8 groups
+            self.i8_meta_per_expert = (((n_blk + 3) // 4 * 16 + 48) * (n_blk > 0)).sum(dim=1).cpu().tolist()
         else:
-            self.i8_mask = self.i8_base = self.i8_hi = None
+            self.i8_mask = self.i8_base = self.i8_hi = self.i8_blocks = self.i8_list = None
 
     def nbytes(self, experts: Optional[Sequence[int]] = None) -> int:
         """Bytes the kernels read for the given experts (all when None)."""
         per = self.rows * self.cols // 2 + self.rows * self.cols // GROUP * 2
         n_exp = self.n_expert if experts is None else len(list(experts))
         n = per * n_exp
-        if self.n_int8:
-            n += self.i8_mask.shape[1] * 4 * 2 * n_exp   # mask + base words
+        if self.n_int8:   # the INT8 list blocks and entries
+            n += sum(int(self.i8_meta_per_expert[e]) for e in (range(self.n_expert) if experts is None else experts))
         return n
 
     def int8_bytes(self, experts: Sequence[int]) -> int:
@@ -257,7 +316,7 @@ class StackedFactor:
         from ._lib import QMatrix
         ptr = lambda t: None if t is None else t.data_ptr()
         return QMatrix(ptr(self.codes), ptr(self.scales), ptr(self.i8_mask), ptr(self.i8_base), ptr(self.i8_hi),
-                       self.rows, self.cols)
+                       ptr(self.i8_blocks), ptr(self.i8_list), self.rows, self.cols)
 
     def expert(self, e: int) -> GroupedFactor:
         """Copy of expert ``e`` as a row-major GroupedFactor (host side; for tests and tooling)."""

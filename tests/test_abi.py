@@ -40,7 +40,7 @@ def test_wait_limit_hook_validates_on_the_host(lib):
 
 
 def test_version_and_status_strings(lib):
-    assert lib.latent_abi_version() == 3
+    assert lib.latent_abi_version() == 4
     assert lib.latent_status_string(0) == b"ok"
     assert b"expert id" in lib.latent_status_string(5)
 

@@ -160,3 +160,41 @@ def test_tile_major_order_of_wide_factors():
         n = int(sel.sum())
         assert np.array_equal(st.i8_hi[first:first + n].numpy(), hi[sel])
         first += n
+
+
+@pytest.mark.parametrize("rows,cols", [(352, 96), (64, 512), (256, 288)])
+def test_int8_block_lists_match_brute_force(rows, cols):
+    """Every INT8 group appears once in its (expert, tile, 128-row block) list,
+    under its column, in row order, with its record index in (expert, q) order."""
+    rng = np.random.default_rng(rows + cols)
+    E, g = 3, rows * cols // 32
+    is_i8 = torch.from_numpy(rng.random((E, g)) < 0.07)
+    is_i8[1] = False                                     # an expert without INT8 groups
+    words, entries = F.int8_block_lists(is_i8, rows, cols)
+    words, entries = words.numpy().astype(np.int64), entries.numpy().astype(np.int64)
+    tiles, rblk = (cols + 255) // 256, (rows + F.BLOCK_ROWS - 1) // F.BLOCK_ROWS
+    assert words.shape == (E * tiles * rblk, F.BLOCK_WORDS)
+    want = {}
+    rec = 0
+    for e in range(E):
+        for q in range(g):
+            c, within = divmod(q, rows * 8)
+            ng = min(cols // 32 - 8 * c, 8)
+            row, gi = divmod(within, ng)
+            if is_i8[e, q]:
+                want.setdefault((e * tiles + c) * rblk + row // F.BLOCK_ROWS, []).append((gi, row % F.BLOCK_ROWS, rec))
+                rec += 1
+    seen = 0
+    for b in range(words.shape[0]):
+        w = words[b]
+        got = want.get(b, [])
+        assert w[0] == 0 and w[8] == len(got) and w[9] % 4 == 0
+        if not got:
+            continue
+        assert w[10] == min(r for _, _, r in got)
+        for j in range(8):
+            col = sorted((row, r) for gi, row, r in got if gi == j)
+            ent = entries[w[9] + w[j]: w[9] + w[j + 1]]
+            assert [(int(v) >> 16, (int(v) & 0xFFFF) + w[10]) for v in ent] == col, (b, j)
+        seen += len(got)
+    assert seen == int(is_i8.sum())
