@@ -87,7 +87,8 @@ constexpr int kOffLoff = kOffIn + kStageRows * 8 * 4;  // the stage's INT8 list 
 constexpr int kOffList = kOffLoff + 64;                // its INT8 list entries (kListCap)
 constexpr int kOffRec = kOffList + kListCap * 4;
 constexpr int kOffHdr = kOffRec + kRecCap * 16;
-constexpr int kSlotBytes = (kOffHdr + 128 + 1023) / 1024 * 1024;
+constexpr int kOffPre = kOffHdr + 128;  // P4 (and weighted P2) first stage: the item's 8 slots and router weights
+constexpr int kSlotBytes = (kOffPre + 64 + 1023) / 1024 * 1024;
 static_assert(kOffHdr % 16 == 0, "slot alignment");
 
 // Dynamic shared memory: region A (barriers, per-warp item data, cross-warp
@@ -602,13 +603,21 @@ __device__ void producer_run(const Args &a, const CodeMaps &maps, const Geo &g, 
     __syncwarp();
 }
 
+// First stage of an item whose epilogue needs its slots and router weights
+// (P4; P2 when the weights scale the down projection's input).
+__device__ __forceinline__ bool needs_pre(const Args &a, const Hdr &h) {
+    return (h.flags & kFirst) && (h.kind == 4 || (h.kind == 2 && (a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN)));
+}
+
 // --- input warp ------------------------------------------------------------------
 // Follows the stage headers in ring order.  P1 stages: the lanes gather the
 // stage's rows of x for the item's tokens, convert them to fp32 and store
 // them as [row][NT] in the slot.  Later phases: once the item's dependency is
 // met (done[phase-1][v] reached its target), one bulk copy of the input rows.
-// Either way the warp then arrives on the slot's barrier (release: the inputs
-// are ordered before the consumers' reads).  On an abort the copy is issued
+// The first stage of a P4 item (and of a P2 item under weight-before-down)
+// also gets the item's slots and router weights (global loads kept off the
+// consumers).  Either way the warp then arrives on the slot's barrier
+// (release: the inputs are ordered before the consumers' reads).  On an abort the copy is issued
 // anyway, so that every byte the slot expects arrives.
 template <int XT>
 __device__ __forceinline__ void gather_rows(const Args &a, const Hdr &h, const int (&tok)[8], uint32_t in, int lane) {
@@ -655,6 +664,15 @@ __device__ void input_run(const Args &a, const Geo &g, const Slots &slot_ptr, ui
         if (h.kind == kStop) {
             if (lane == 0) mbar_arrive(full);
             return;
+        }
+        if (needs_pre(a, h)) {  // the item's slots and router weights, staged for the consumers' epilogue
+            if (lane < 8) {
+                const int sl = lane < h.nt ? __ldg(&a.order[h.first_pos + lane]) : 0;
+                int *pre = reinterpret_cast<int *>(const_cast<uint8_t *>(sp) + kOffPre);
+                pre[lane] = sl;
+                pre[8 + lane] = __float_as_int(lane < h.nt ? load_weight(a.weights, a.w_type, sl) : 0.f);
+            }
+            __syncwarp();  // before lane 0's arrival on the slot
         }
         if (h.kind == 1) {
             if (h.v != tok_v) {
@@ -982,14 +1000,8 @@ __device__ void consumer_run(const Args &a, const Slots &slot_ptr, uint32_t bars
             release_pending(a, wc);
             return;
         }
-        if ((h.flags & kFirst) && (h.kind == 4 || (h.kind == 2 && (a.flags & LATENT_FLAG_WEIGHT_BEFORE_DOWN)))) {
-            // the item's slots and router weights, loaded now and read by its epilogue
-            if (lane < 8) {
-                const int sl = lane < h.nt ? __ldg(&a.order[h.first_pos + lane]) : 0;
-                wc.pre[lane] = sl;
-                wc.pre[8 + lane] = __float_as_int(lane < h.nt ? load_weight(a.weights, a.w_type, sl) : 0.f);
-            }
-        }
+        if (needs_pre(a, h) && lane < 16)  // the item's slots and router weights, read by its epilogue
+            wc.pre[lane] = reinterpret_cast<const int *>(sp + kOffPre)[lane];
         int g, rp, P, rr0, rr1;
         warp_part(wc.w, h.ng, h.nrows, g, rp, P, rr0, rr1);
         if (g >= 0) {
@@ -1200,10 +1212,10 @@ void decode_bind_scratch(DecodeArgs &a, float *f) {
     a.sb = f;
 }
 
-// K-chunk rows of the split phases: about 64 KB of codes and scales per item.
-static int chunk_rows(int K, int tile_w) {
+// K-chunk rows of the split phases: about `bytes` of codes and scales per item.
+static int chunk_rows(int K, int tile_w, double bytes) {
     const double bytes_per_row = tile_w * 0.5625;
-    int stages = (int)(65536.0 / (bytes_per_row * kStageRows) + 0.5);
+    int stages = (int)(bytes / (bytes_per_row * kStageRows) + 0.5);
     if (stages < 1) stages = 1;
     if (stages > 32) stages = 32;  // the producer keeps one stage's metadata per lane
     int rows = stages * kStageRows;
@@ -1335,8 +1347,14 @@ cudaError_t launch_decode(const DecodeArgs &d, cudaStream_t s, Marks *marks) {
     a.tb = d.tb;
     a.hb = d.hb;
     a.sb = d.sb;
-    a.chunk1 = chunk_rows(d.d, d.r < 256 ? d.r : 256);
-    a.chunk3 = chunk_rows(d.f, d.r < 256 ? d.r : 256);
+    // With >= 128 active experts possible there are items enough for every CTA
+    // at 256 KB per item, which cuts the per-item epilogues and split-K adds
+    // (config 4 at batch 64 / 256: -7.5% / -6%); with fewer, 64 KB items keep
+    // the CTAs balanced (config 1 at 128 KB: +6%; batch 1 and 8 gain nothing
+    // from 16 or 32 KB items).
+    const double item_bytes = d.nmax >= 128 ? 262144.0 : 65536.0;
+    a.chunk1 = chunk_rows(d.d, d.r < 256 ? d.r : 256, item_bytes);
+    a.chunk3 = chunk_rows(d.f, d.r < 256 ? d.r : 256, item_bytes);
     a.wait_ns = g_wait_ns.load();
     a.dep_extra = g_dep_extra.load();
     CodeMaps maps;
