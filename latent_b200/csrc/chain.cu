@@ -87,7 +87,7 @@ constexpr int kOffLoff = kOffIn + kStageRows * 8 * 4;  // the stage's INT8 list 
 constexpr int kOffList = kOffLoff + 64;                // its INT8 list entries (kListCap)
 constexpr int kOffRec = kOffList + kListCap * 4;
 constexpr int kOffHdr = kOffRec + kRecCap * 16;
-constexpr int kOffPre = kOffHdr + 128;  // P4 (and weighted P2) first stage: the item's 8 slots and router weights
+constexpr int kOffPre = kOffHdr + 128;  // P4 (and weighted P2) first stage: the item's 8 output rows and router weights
 constexpr int kSlotBytes = (kOffPre + 64 + 1023) / 1024 * 1024;
 static_assert(kOffHdr % 16 == 0, "slot alignment");
 
@@ -669,7 +669,8 @@ __device__ void input_run(const Args &a, const Geo &g, const Slots &slot_ptr, ui
             if (lane < 8) {
                 const int sl = lane < h.nt ? __ldg(&a.order[h.first_pos + lane]) : 0;
                 int *pre = reinterpret_cast<int *>(const_cast<uint8_t *>(sp) + kOffPre);
-                pre[lane] = sl;
+                // the output row: the slot's own row, or its token's for the combined output
+                pre[lane] = (a.flags & LATENT_FLAG_OUT_PER_SLOT) ? sl : sl / a.k;
                 pre[8 + lane] = __float_as_int(lane < h.nt ? load_weight(a.weights, a.w_type, sl) : 0.f);
             }
             __syncwarp();  // before lane 0's arrival on the slot
@@ -731,9 +732,8 @@ struct Cfg {
 struct Warp {
     int w, lane;
     uint32_t lb;      // replica bits of the lookup address
-    uint32_t list;    // shared address of the warp's INT8 row list (kStageRows entries)
     uint8_t *xbuf;
-    int *pre;         // [8] slots, [8] router weights (float bits) of the current item's tokens
+    int *pre;         // [8] output rows, [8] router weights (float bits) of the current item's tokens
     bool zeroed;      // the kernel-start zeroing is known complete
     int pend_kind, pend_v;  // completion count not yet released
     uint32_t xbar, xpar;    // the consumer warps' barrier and the phase this warp waits for next
@@ -932,11 +932,11 @@ __device__ __forceinline__ void epilogue(const Args &a, const Hdr &h, int col, c
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
             if (t < h.nt) {
-                const int slot = pre[t];
+                const int orow = pre[t];  // output row (slot, or token of the combined output)
                 if (per_slot) {
-                    a.out[(int64_t)slot * a.d + gc] = g[t];
+                    a.out[(int64_t)orow * a.d + gc] = g[t];
                 } else {
-                    float *o = a.out + (int64_t)(slot / a.k) * a.d + gc;
+                    float *o = a.out + (int64_t)orow * a.d + gc;
                     const float y = wbd ? g[t] : __int_as_float(pre[8 + t]) * g[t];
                     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(o), "f"(y) : "memory");
                 }
@@ -948,6 +948,14 @@ __device__ __forceinline__ void epilogue(const Args &a, const Hdr &h, int col, c
 // Group and row part of warp w for a tile of ng groups; rows [rr0, rr1) of a
 // stage of n rows.  Warps past G * P have no columns (ng not a power of two).
 __device__ __forceinline__ void warp_part(int w, int ng, int n, int &g, int &rp, int &P, int &rr0, int &rr1) {
+    if (ng == kNW) {  // full tiles: one warp per group, every row (no divisions)
+        P = 1;
+        g = w;
+        rp = 0;
+        rr0 = 0;
+        rr1 = n;
+        return;
+    }
     P = kNW / ng;
     if (P < 1) P = 1;
     g = w % ng;
