@@ -724,6 +724,7 @@ __device__ void input_run(const Args &a, const Geo &g, const Slots &slot_ptr, ui
 template <int NT>
 struct Cfg {
     static constexpr int CPL = NT == 4 ? 16 : 8;  // columns per lane
+    static_assert(NT == 4 || NT == 8, "token columns");
     static constexpr int LPR = 32 / CPL;           // lanes per 32-column group row
     static constexpr int S = 32 / LPR;             // row slots per warp
     static constexpr int NB = CPL / 2;             // code bytes per lane and row
@@ -956,6 +957,17 @@ __device__ __forceinline__ void warp_part(int w, int ng, int n, int &g, int &rp,
         rr1 = n;
         return;
     }
+    if ((ng & (ng - 1)) == 0) {  // 1, 2 or 4 groups: shifts
+        const int lg = __ffs(ng) - 1;
+        P = kNW >> lg;
+        g = w & (ng - 1);
+        rp = w >> lg;
+        const int lp = __ffs(P) - 1;
+        const int per = (n + P - 1) >> lp;
+        rr0 = min(n, rp * per);
+        rr1 = min(n, rr0 + per);
+        return;
+    }
     P = kNW / ng;
     if (P < 1) P = 1;
     g = w % ng;
@@ -1080,9 +1092,10 @@ __device__ void consumer_run(const Args &a, const Slots &slot_ptr, uint32_t bars
             wc.zeroed = true;
         }
         if (g >= 0 && rp == 0) {
-            const int lpr = h.NT == 4 ? Cfg<4>::LPR : Cfg<8>::LPR;
+            // lane (rs, ch) holds column ch * CPL + rs (LPR = 2 or 4: shifts, not divisions)
+            const int llpr = h.NT == 4 ? 1 : 2;  // log2(Cfg<NT>::LPR)
             const int cpl = h.NT == 4 ? Cfg<4>::CPL : Cfg<8>::CPL;
-            const int col = 32 * g + (lane % lpr) * cpl + lane / lpr;
+            const int col = 32 * g + (lane & ((1 << llpr) - 1)) * cpl + (lane >> llpr);
             if (col < h.tile_w) {
                 if (h.NT == 4)
                     epilogue<4>(a, h, col, gv, uv, wc.pre);
