@@ -23,8 +23,8 @@
 //
 // CTA.  One persistent CTA per SM (cooperative launch: every CTA is resident,
 // which the zeroing at kernel start relies on), three roles:
-//  - the producer warp takes items two ahead, loads their virtual-expert
-//    entry and INT8 record boundaries while it issues earlier items, and
+//  - the producer warp takes items one at a time from the queue, loads their
+//    virtual-expert entry and INT8 list blocks, and
 //    fills a ring of kSlots stages (128 rows of one tile) with cp.async.bulk
 //    copies completing on the slot's mbarrier: codes, scales, INT8 records
 //    and the stage's INT8 list block.  Weight copies never wait for a
@@ -429,12 +429,15 @@ __device__ MetaRaw meta_load(const Args &a, const Item &it, int lane) {
 }
 
 // --- producer --------------------------------------------------------------------
-// Items come from the counter two ahead of their issue: while item i is
-// issued, the index of item i+2 is on its way, the virtual-expert entry of
-// item i+1 has arrived and its INT8 boundary words are being loaded, so the
-// producer waits for memory only when the ring is full.  Every CTA handles its
-// items in counter order and every dependency points to a lower item, so the
-// lowest unfinished item is always at the head of some CTA: no deadlock.
+// Items come from the counter one at a time: the next index is claimed once
+// the current item's last stage has a slot, and its virtual-expert entry and
+// INT8 block words are loaded after that stage is issued, while the ring
+// (up to kSlots stages) keeps the consumers busy.  Claiming later keeps the
+// end of the queue balanced: a CTA holds no item it cannot start soon (items
+// claimed two ahead left CTAs idle at the end while others still held
+// several: config 1 136 -> 126 us).  Every CTA handles its items in counter
+// order and every dependency points to a lower item, so the lowest unfinished
+// item is always at the head of some CTA: no deadlock.
 __device__ __forceinline__ int mat_index(int phase, int m) { return phase == 1 ? m : phase == 2 ? 2 + m : phase == 3 ? 4 : 5; }
 
 // One expert's view of a stacked factor, held in registers by the producer.
@@ -475,35 +478,15 @@ __device__ void producer_run(const Args &a, const CodeMaps &maps, const Geo &g, 
     int q = 0;
     if (lane == 0) q = (int)atomicAdd(a.queue, 1u);
     const int i0 = __shfl_sync(0xffffffffu, q, 0);
-    if (lane == 0) q = (int)atomicAdd(a.queue, 1u);
-    const int i1 = __shfl_sync(0xffffffffu, q, 0);
-    Item cur{}, nxt{};
+    Item cur{};
     MetaRaw mc{0u, 0u, 0u, 0u};
-    bool have_cur = i0 < total, have_nxt = i1 < total;
+    bool have_cur = i0 < total;
     if (have_cur) {
         cur = item_shape(a, g, i0);
         cur.ve = __ldg(&a.virt[cur.v]);
         mc = meta_load(a, cur, lane);
     }
-    if (have_nxt) {
-        nxt = item_shape(a, g, i1);
-        nxt.ve = __ldg(&a.virt[nxt.v]);
-    }
-    if (lane == 0 && have_nxt) q = (int)atomicAdd(a.queue, 1u);  // the item after nxt
     while (have_cur && ok) {
-        MetaRaw mn{0u, 0u, 0u, 0u};
-        Item nn{};
-        bool have_nn = false;
-        if (have_nxt) {
-            mn = meta_load(a, nxt, lane);  // nxt.ve arrived during the last item
-            const int i2 = __shfl_sync(0xffffffffu, q, 0);
-            have_nn = i2 < total;
-            if (have_nn) {
-                nn = item_shape(a, g, i2);
-                nn.ve = __ldg(&a.virt[nn.v]);
-                if (lane == 0) q = (int)atomicAdd(a.queue, 1u);
-            }
-        }
         const int ph = cur.phase;
         const int4 ve = cur.ve;
         const int NT = ve.z <= 4 ? 4 : 8;
@@ -519,6 +502,8 @@ __device__ void producer_run(const Args &a, const CodeMaps &maps, const Geo &g, 
             if (lane == 0) ok = mbar_wait(empty, (empty_par >> slot) & 1u, a.err, a.wait_ns);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
+            // the next item is claimed once the last stage of this one has a slot
+            if (lane == 0 && s == cur.n_stages - 1) q = (int)atomicAdd(a.queue, 1u);
             const uint32_t sbase = smem_u32(slot_ptr[slot]);
             int m = 0, row0 = 0, n = 0;
             stage_rows(cur, s, m, row0, n);
@@ -576,11 +561,14 @@ __device__ void producer_run(const Args &a, const CodeMaps &maps, const Geo &g, 
             empty_par ^= 1u << slot;
             slot = slot + 1 == kSlots ? 0 : slot + 1;
         }
-        cur = nxt;
-        mc = mn;
-        have_cur = have_nxt;
-        nxt = nn;
-        have_nxt = have_nn;
+        if (!ok) break;
+        const int i1 = __shfl_sync(0xffffffffu, q, 0);
+        have_cur = i1 < total;
+        if (have_cur) {
+            cur = item_shape(a, g, i1);
+            cur.ve = __ldg(&a.virt[cur.v]);
+            mc = meta_load(a, cur, lane);
+        }
     }
     if (lane == 0) {
         if (ok && mbar_wait(empty0 + 8 * slot, (empty_par >> slot) & 1u, a.err, a.wait_ns)) {
@@ -1233,10 +1221,9 @@ void decode_bind_scratch(DecodeArgs &a, float *f) {
     a.sb = f;
 }
 
-// K-chunk rows of the split phases: about `bytes` of codes and scales per item.
-static int chunk_rows(int K, int tile_w, double bytes) {
-    const double bytes_per_row = tile_w * 0.5625;
-    int stages = (int)(bytes / (bytes_per_row * kStageRows) + 0.5);
+// K-chunk rows of the split phases: chunks of about `stages` stages, even,
+// multiples of the stage rows.
+static int chunk_rows(int K, int stages) {
     if (stages < 1) stages = 1;
     if (stages > 32) stages = 32;  // the producer keeps one stage's metadata per lane
     int rows = stages * kStageRows;
@@ -1368,14 +1355,16 @@ cudaError_t launch_decode(const DecodeArgs &d, cudaStream_t s, Marks *marks) {
     a.tb = d.tb;
     a.hb = d.hb;
     a.sb = d.sb;
-    // With >= 128 active experts possible there are items enough for every CTA
-    // at 256 KB per item, which cuts the per-item epilogues and split-K adds
-    // (config 4 at batch 64 / 256: -7.5% / -6%); with fewer, 64 KB items keep
-    // the CTAs balanced (config 1 at 128 KB: +6%; batch 1 and 8 gain nothing
-    // from 16 or 32 KB items).
-    const double item_bytes = d.nmax >= 128 ? 262144.0 : 65536.0;
-    a.chunk1 = chunk_rows(d.d, d.r < 256 ? d.r : 256, item_bytes);
-    a.chunk3 = chunk_rows(d.f, d.r < 256 ? d.r : 256, item_bytes);
+    // K-chunks: about four P1 items per CTA for the active experts the batch
+    // can have.  Longer items cut the per-item epilogues and split-K adds,
+    // shorter ones keep the CTAs busy to the end (config 1: 4 x 512 rows;
+    // config 4 rank 256 at batch 1 / 64: 28 x 256 / 2 x 3584 rows).  P3
+    // takes chunks of the same size.
+    const int nact = d.nmax > 0 ? d.nmax : 1;
+    const int kc1 = (4 * grid + 2 * nact - 1) / (2 * nact);
+    const int st = ((d.d + kc1 - 1) / kc1 + kStageRows - 1) / kStageRows;
+    a.chunk1 = chunk_rows(d.d, st);
+    a.chunk3 = chunk_rows(d.f, st);
     a.wait_ns = g_wait_ns.load();
     a.dep_extra = g_dep_extra.load();
     CodeMaps maps;
