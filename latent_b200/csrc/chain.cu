@@ -278,11 +278,6 @@ __device__ __forceinline__ uint32_t lds16(uint32_t addr) {
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
     return v;
 }
-__device__ __forceinline__ uint32_t lds8(uint32_t addr) {
-    unsigned short v;
-    asm volatile("ld.shared.u8 %0, [%1];" : "=h"(v) : "r"(addr));
-    return v;
-}
 __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
     float4 v;
     asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));

@@ -137,14 +137,11 @@ __global__ void __launch_bounds__(256) k_pf_gather(const void *x, const int32_t 
 
 // mtile_off[e] = sum over e' < e of ceil(count[e'] / 128); mtile_off[E] = total.
 __global__ void __launch_bounds__(1024) k_pf_mtiles(const int32_t *counts, int E, int32_t *mtile_off) {
-    __shared__ int part[1024];
     __shared__ int warp_sum[32];
     const int per = (E + 1023) / 1024;
     const int lo = min(E, (int)threadIdx.x * per), hi = min(E, lo + per);
     int s = 0;
     for (int e = lo; e < hi; ++e) s += (counts[e] + kBM - 1) / kBM;
-    part[threadIdx.x] = s;
-    __syncthreads();
     // inclusive scan over 1024 partials (warp shuffles, then warp totals)
     int v = s;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
