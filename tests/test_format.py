@@ -198,3 +198,22 @@ def test_int8_block_lists_match_brute_force(rows, cols):
             assert [(int(v) >> 16, (int(v) & 0xFFFF) + w[10]) for v in ent] == col, (b, j)
         seen += len(got)
     assert seen == int(is_i8.sum())
+
+
+def test_int8_metadata_bytes_follow_the_block_lists():
+    """nbytes counts what the decode kernel stages for INT8: 48 bytes of block
+    words plus the padded entries of every block holding INT8 groups."""
+    rng = np.random.default_rng(8)
+    fs = []
+    for e in range(3):
+        v = rng.standard_normal((160, 288)).astype(np.float32)
+        v[:, 5 + e] *= 60.0
+        fs.append(quantize_factor(torch.from_numpy(v), 20.0))
+    st = F.StackedFactor(fs, "cpu")
+    assert st.n_int8 > 0
+    words = st.i8_blocks.numpy().astype(np.int64)
+    per_block = np.where(words[:, 8] > 0, 48 + (words[:, 8] + 3) // 4 * 16, 0).reshape(3, -1)
+    base = 160 * 288 // 2 + 160 * 288 // 32 * 2
+    for e in range(3):
+        assert st.nbytes([e]) == base + int(per_block[e].sum())
+    assert st.nbytes() == 3 * base + int(per_block.sum())
